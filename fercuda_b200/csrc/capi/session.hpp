@@ -1,0 +1,127 @@
+// Internal state behind fer_session_t.
+//
+// Mirrors the reference RuntimeSession (src/runtime/session.cu:62-416),
+// RegimeManager (regime_manager.cu:15-123), ElasticPool (elastic_pool.cu:37-131)
+// and JobManager (job_manager.cu:23-92) in one object:
+//   - buffers: id -> record, ids from a counter starting at 1;
+//   - regimes: builtin CUSTOM_POOL (this session's TLSF pool), CUDA_MALLOC,
+//     CUDA_MANAGED, plus registered custom allocators;
+//   - jobs: an event recorded on the session stream plus the temporaries to
+//     release once the event is observed complete; events are pooled;
+//   - one session stream (the pool runtime's stream 0, non-blocking).
+// Like the reference, a session is used from one thread at a time.
+#pragma once
+
+#include "fercuda/api/c_api.h"
+#include "fercuda/b200/ext.h"
+#include "fercuda/jit/api.h"
+#include "gpu/gpu_hot_runtime.h"
+
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace fer::capi {
+
+inline fer_status_t ok() { return fer_status_t{FER_STATUS_OK, "ok"}; }
+inline fer_status_t invalid(const char* m) { return fer_status_t{FER_STATUS_INVALID_ARGUMENT, m}; }
+inline fer_status_t not_found(const char* m) { return fer_status_t{FER_STATUS_NOT_FOUND, m}; }
+inline fer_status_t internal(const char* m) { return fer_status_t{FER_STATUS_INTERNAL_ERROR, m}; }
+
+size_t dtype_size(uint32_t dtype);
+
+struct Buffer {
+    void* ptr = nullptr;
+    fer_buffer_desc_t desc{};
+    size_t numel = 0;
+    size_t bytes = 0;
+    uint32_t regime = 0;
+    uint32_t tier = 0;
+    bool external = false;
+    fer_external_buffer_deleter_fn deleter = nullptr;
+    void* deleter_ctx = nullptr;
+};
+
+struct Temp {
+    void* ptr;
+    uint32_t regime;
+    uint32_t tier;
+    size_t bytes;
+};
+
+struct Job {
+    cudaEvent_t ev = nullptr;   // null once finalized
+    std::vector<Temp> temps;
+    bool finalized = false;
+};
+
+struct CustomAlloc {
+    fer_allocator_alloc_fn alloc = nullptr;
+    fer_allocator_free_fn free = nullptr;
+    void* ctx = nullptr;
+    // gpu_hot-style registration
+    fer_gpu_hot_alloc_fn hot_alloc = nullptr;
+    fer_gpu_hot_free_fn hot_free = nullptr;
+    void* runtime = nullptr;
+};
+
+class JitManager;
+
+struct Session {
+    int device = 0;
+    fer_pool_config_t cfg{};
+    GPUHotRuntime* pool = nullptr;
+    cudaStream_t stream = nullptr;
+    uint32_t default_regime = FER_MEMORY_CUSTOM_POOL;
+    std::unordered_map<uint32_t, CustomAlloc> custom;
+    std::unordered_map<uint64_t, Buffer> buffers;
+    uint64_t next_buffer = 1;
+    std::unordered_map<uint64_t, Job> jobs;
+    uint64_t next_job = 1;
+    std::vector<cudaEvent_t> spare_events;
+    size_t live_bytes[2] = {0, 0};   // CUDA_MALLOC / MANAGED budget per tier
+    uint32_t* dev_err = nullptr;     // device error word (cudaMalloc'd)
+    std::unique_ptr<JitManager> jit;
+
+    ~Session();
+
+    // Regimes and memory.
+    fer_status_t resolve_regime(uint32_t requested, uint32_t* out) const;
+    fer_status_t alloc_bytes(size_t bytes, uint32_t tier, uint32_t tag, uint32_t regime, void** out);
+    fer_status_t free_bytes(void* ptr, uint32_t regime, uint32_t tier, size_t bytes);
+    fer_status_t alloc_temp(size_t bytes, uint32_t regime, Temp* out);
+
+    // Buffers.
+    const Buffer* find(uint64_t id) const;
+    fer_status_t add_buffer(const fer_buffer_desc_t& d, void* ptr, uint32_t regime, bool external,
+                            fer_external_buffer_deleter_fn del, void* del_ctx, uint64_t* out_id);
+
+    // Jobs: records completion of everything queued so far on the stream.
+    fer_status_t make_job(std::vector<Temp> temps, uint64_t* out_job);
+    fer_status_t finalize(uint64_t id, bool* done);
+};
+
+// Validates a buffer descriptor (rank 1..4, known dtype, nonzero size).
+fer_status_t check_desc(const fer_buffer_desc_t& d, size_t* numel, size_t* bytes);
+
+}  // namespace fer::capi
+
+struct fer_session {
+    fer::capi::Session impl;
+};
+
+// Kernel launchers exported by libptx_kernels.so.
+extern "C" {
+cudaError_t fer_rows_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
+                         float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
+cudaError_t fer_matmul_ref_order(const void* a, const void* b, void* c, int M, int K, int N, uint32_t dtype,
+                                 cudaStream_t stream);
+cudaError_t fer_cast_to_f32(const void* in, float* out, size_t n, uint32_t dtype, cudaStream_t stream);
+cudaError_t fer_cast_from_f32(const float* in, void* out, size_t n, uint32_t dtype, cudaStream_t stream);
+cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K, uint32_t out_dtype,
+                             uint32_t* err, cudaStream_t stream);
+}

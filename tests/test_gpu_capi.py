@@ -1,0 +1,346 @@
+"""The reference's C-API tests (tests/c_api/*.cpp), restated in Python over
+the same entry points, plus matmul parity with the reference's own GEMM
+kernel (oracle/_ref) on the same device buffers."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from fercuda_b200 import capi, synth
+from tests import oracle_lib
+
+pytestmark = pytest.mark.gpu
+
+
+def f16(x):
+    return np.asarray(x, np.float16).view(np.uint16)
+
+
+def test_bridge_matmul_and_layer_norm_all_dtypes(session):
+    """test_c_api_bridge.cpp: 2x2 matmul {19,22,43,50} for f32 (1e-5), f16
+    (5e-2), bf16 (2e-1), i8/u8 (exact); dtype mismatch rejected."""
+    a, b = [1, 2, 3, 4], [5, 6, 7, 8]
+    golden = np.array([19, 22, 43, 50], np.float32)
+    cases = [(capi.FER_DTYPE_F32, np.float32, 1e-5), (capi.FER_DTYPE_F16, np.float16, 5e-2),
+             (capi.FER_DTYPE_BF16, None, 2e-1), (capi.FER_DTYPE_I8, np.int8, 0), (capi.FER_DTYPE_U8, np.uint8, 0)]
+    for dt, npdt, tol in cases:
+        ba, bb, bo = (session.alloc(dt, [2, 2]) for _ in range(3))
+        if dt == capi.FER_DTYPE_BF16:
+            ha, hb = synth.f32_to_bf16_bits(np.array(a, np.float32)), synth.f32_to_bf16_bits(np.array(b, np.float32))
+        else:
+            ha, hb = np.array(a, npdt), np.array(b, npdt)
+        session.upload(ba, ha)
+        session.upload(bb, hb)
+        session.wait(session.matmul(ba, bb, bo))
+        out = np.empty(4, np.uint16 if dt == capi.FER_DTYPE_BF16 else npdt)
+        session.download(bo, out)
+        got = synth.bf16_bits_to_f32(out) if dt == capi.FER_DTYPE_BF16 else out.astype(np.float32)
+        assert np.abs(got - golden).max() <= tol, (dt, got)
+    ba = session.alloc(capi.FER_DTYPE_F16, [2, 2])
+    bb = session.alloc(capi.FER_DTYPE_F32, [2, 2])
+    bo = session.alloc(capi.FER_DTYPE_F16, [2, 2])
+    with pytest.raises(capi.FerError) as e:
+        session.matmul(ba, bb, bo)
+    assert e.value.code == capi.FER_STATUS_INVALID_ARGUMENT
+    # layer norm in f16 / bf16 through the cast staging
+    x = np.array([1, 2, 3, 4], np.float32)
+    ref = (x - x.mean()) / np.sqrt(((x - x.mean()) ** 2).mean() + 1e-6)
+    for dt, host, tol in [(capi.FER_DTYPE_F16, f16(x), 7e-2), (capi.FER_DTYPE_BF16, synth.f32_to_bf16_bits(x), 2e-1)]:
+        bx, by = session.alloc(dt, [4]), session.alloc(dt, [4])
+        session.upload(bx, host)
+        job = C.c_uint64()
+        req = capi.fer_layer_norm_request_t(bx, by, 1e-6, capi.FER_MEMORY_AUTO)
+        capi.check("ln", session.call("fer_submit_layer_norm", C.byref(req), C.byref(job)))
+        session.wait(job.value)
+        out = np.empty(4, np.uint16)
+        session.download(by, out)
+        got = out.view(np.float16).astype(np.float32) if dt == capi.FER_DTYPE_F16 else synth.bf16_bits_to_f32(out)
+        assert np.abs(got - ref).max() <= tol
+
+
+@pytest.mark.parametrize("m,k,n", [(2, 2, 2), (1, 1, 1), (17, 33, 65), (128, 128, 128), (129, 257, 131),
+                                   (300, 1000, 200), (512, 48, 512)])
+def test_matmul_f32_bit_exact_vs_reference_kernel(session, m, k, n):
+    ref = oracle_lib.ref_kernels()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    a = synth.normal_f32(41, m * k).reshape(m, k)
+    b = synth.normal_f32(42, k * n).reshape(k, n)
+    ba, bb = session.alloc(capi.FER_DTYPE_F32, [m, k]), session.alloc(capi.FER_DTYPE_F32, [k, n])
+    bo, br = session.alloc(capi.FER_DTYPE_F32, [m, n]), session.alloc(capi.FER_DTYPE_F32, [m, n])
+    session.upload(ba, a)
+    session.upload(bb, b)
+    session.wait(session.matmul(ba, bb, bo))
+    ref.refshim_matmul_f32(C.c_void_p(session.ptr_of(ba)), C.c_void_p(session.ptr_of(bb)),
+                           C.c_void_p(session.ptr_of(br)), m, k, n, C.c_void_p(session.stream()))
+    y, yr = np.empty((m, n), np.float32), np.empty((m, n), np.float32)
+    session.download(bo, y)
+    session.download(br, yr)
+    assert np.array_equal(y.view(np.uint32), yr.view(np.uint32))
+    # CPU oracle: same sequential fmaf chain, bit-exact
+    yo = np.empty((m, n), np.float32)
+    oracle_lib.load().orc_matmul_f32(oracle_lib.ptr(a), oracle_lib.ptr(b), oracle_lib.ptr(yo), m, k, n, 0, m, 4)
+    assert np.array_equal(y.view(np.uint32), yo.view(np.uint32))
+    for x in (ba, bb, bo, br):
+        session.free(x)
+
+
+def test_matmul_bf16_matches_reference_cast_path(session):
+    """bf16 fer_submit_matmul = the reference's cast -> f32 GEMM -> cast back,
+    bit for bit (the conversions happen inside the kernel here)."""
+    ref = oracle_lib.ref_kernels()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    m, k, n = 96, 160, 80
+    a = synth.normal_bf16(43, m * k).reshape(m, k)
+    b = synth.normal_bf16(44, k * n).reshape(k, n)
+    ba, bb, bo = session.alloc(capi.FER_DTYPE_BF16, [m, k]), session.alloc(capi.FER_DTYPE_BF16, [k, n]), \
+        session.alloc(capi.FER_DTYPE_BF16, [m, n])
+    session.upload(ba, a)
+    session.upload(bb, b)
+    session.wait(session.matmul(ba, bb, bo))
+    y = np.empty((m, n), np.uint16)
+    session.download(bo, y)
+    fa, fb, fo = (session.alloc(capi.FER_DTYPE_F32, s) for s in ([m, k], [k, n], [m, n]))
+    session.upload(fa, synth.bf16_bits_to_f32(a))
+    session.upload(fb, synth.bf16_bits_to_f32(b))
+    ref.refshim_matmul_f32(C.c_void_p(session.ptr_of(fa)), C.c_void_p(session.ptr_of(fb)),
+                           C.c_void_p(session.ptr_of(fo)), m, k, n, C.c_void_p(session.stream()))
+    yf = np.empty((m, n), np.float32)
+    session.download(fo, yf)
+    assert np.array_equal(y, synth.f32_to_bf16_bits(yf))
+
+
+def test_matmul_shape_and_id_errors(session):
+    ba = session.alloc(capi.FER_DTYPE_F32, [4, 3])
+    bb = session.alloc(capi.FER_DTYPE_F32, [4, 3])
+    bo = session.alloc(capi.FER_DTYPE_F32, [4, 3])
+    with pytest.raises(capi.FerError) as e:
+        session.matmul(ba, bb, bo)
+    assert e.value.code == capi.FER_STATUS_INVALID_ARGUMENT
+    with pytest.raises(capi.FerError) as e:
+        session.matmul(ba, 123456789, bo)
+    assert e.value.code == capi.FER_STATUS_NOT_FOUND
+
+
+def _jit_compile(session, src, mode=capi.FER_JIT_MODE_STRICT):
+    s = capi.fer_jit_source_t(capi.FER_JIT_SOURCE_CUDA, src.encode(), len(src))
+    o = capi.fer_jit_options_t(capi.FER_JIT_BACKEND_NVRTC, mode, None, None, None, 0)
+    prog = C.c_void_p()
+    res = capi.fer_jit_compile_result_t()
+    st = session.call("fer_jit_compile", C.byref(s), C.byref(o), C.byref(prog), C.byref(res))
+    return st, prog, res
+
+
+def _wild(kind):
+    d = capi.fer_jit_arg_desc_t()
+    d.kind = kind
+    d.expected_dtype = capi.FER_JIT_WILDCARD_U32
+    d.expected_rank = capi.FER_JIT_WILDCARD_U32
+    d.expected_bytes = capi.FER_JIT_WILDCARD_U64
+    for i in range(4):
+        d.expected_dims[i] = capi.FER_JIT_WILDCARD_U32
+    return d
+
+
+def test_jit_exec_add_scalar(session):
+    """test_c_api_jit_exec.cpp: NVRTC vector add with contract descriptors."""
+    n = 256
+    buf = session.alloc(capi.FER_DTYPE_F32, [n])
+    session.upload(buf, np.full(n, 1.5, np.float32))
+    src = ('extern "C" __global__ void add_scalar(float* x, float v, unsigned int n) {'
+           '  unsigned int i = blockIdx.x * blockDim.x + threadIdx.x;  if (i < n) x[i] += v; }')
+    st, prog, res = _jit_compile(session, src)
+    assert st.code == 0, res.log
+    descs = (capi.fer_jit_arg_desc_t * 3)(_wild(capi.FER_JIT_ARG_BUFFER), _wild(capi.FER_JIT_ARG_SCALAR_F32),
+                                         _wild(capi.FER_JIT_ARG_SCALAR_U32))
+    descs[0].access = capi.FER_JIT_ACCESS_READ_WRITE
+    descs[0].expected_dtype = capi.FER_DTYPE_F32
+    descs[0].expected_rank = 1
+    descs[0].expected_bytes = n * 4
+    descs[0].expected_dims[0] = n
+    sig = capi.fer_jit_kernel_sig_t(descs, 3)
+    kern = C.c_void_p()
+    capi.check("get_kernel", session.call("fer_jit_get_kernel", prog, b"add_scalar", C.byref(sig), C.byref(kern)))
+    vals = (capi.fer_jit_arg_value_t * 3)()
+    vals[0].kind, vals[0].as_.buffer_id = capi.FER_JIT_ARG_BUFFER, buf
+    vals[1].kind, vals[1].as_.f32 = capi.FER_JIT_ARG_SCALAR_F32, 2.25
+    vals[2].kind, vals[2].as_.u32 = capi.FER_JIT_ARG_SCALAR_U32, n
+    pack = capi.fer_jit_arg_pack_t(vals, 3)
+    cfg = capi.fer_jit_launch_cfg_t(2, 1, 1, 128, 1, 1, 0, 0)
+    job = C.c_uint64()
+    capi.check("launch", session.call("fer_jit_launch", kern, C.byref(cfg), C.byref(pack), C.byref(job)))
+    session.wait(job.value)
+    out = np.empty(n, np.float32)
+    session.download(buf, out)
+    assert np.all(np.abs(out - 3.75) <= 1e-5)
+    stats = capi.fer_jit_stats_t()
+    capi.check("stats", session.call("fer_jit_get_stats", C.byref(stats)))
+    assert stats.compile_count >= 1 and stats.launch_count >= 1
+    # contract violation: wrong expected rank
+    bad = (capi.fer_jit_arg_desc_t * 3)(descs[0], descs[1], descs[2])
+    bad[0].expected_rank = 2
+    badsig = capi.fer_jit_kernel_sig_t(bad, 3)
+    k2 = C.c_void_p()
+    capi.check("get_kernel", session.call("fer_jit_get_kernel", prog, b"add_scalar", C.byref(badsig), C.byref(k2)))
+    st = session.call("fer_jit_launch", k2, C.byref(cfg), C.byref(pack), C.byref(job))
+    assert st.code == capi.FER_STATUS_INVALID_ARGUMENT
+    # unknown kernel name
+    st = session.call("fer_jit_get_kernel", prog, b"nope", C.byref(sig), C.byref(k2))
+    assert st.code == capi.FER_STATUS_NOT_FOUND
+    # second compile of the same source hits the cache
+    st, prog2, res2 = _jit_compile(session, src)
+    assert st.code == 0 and res2.cache_hit == 1
+    for p in (prog, prog2):
+        session.call("fer_jit_release_program", p)
+
+
+def test_jit_lowering_contracts(session):
+    """test_c_api_jit_lowering.cpp: impossible SM rejected; fusion notes in log.
+    Here the fused kernel the lowering generates is also compiled and run."""
+    st, _, _ = _jit_compile(session, '// fercuda:require_sm>=99\nextern "C" __global__ void k(float* x){}\n')
+    if st.code == 0:
+        pytest.skip("device reports sm >= 99")
+    src = ("// fercuda:fuse=elementwise_chain\n// fercuda:ir_node=elementwise_relu\n"
+           "// fercuda:ir_node=elementwise_sigmoid\n"
+           'extern "C" __global__ void k(float* x){ if(threadIdx.x==0) x[0]+=1.0f; }\n')
+    st, prog, res = _jit_compile(session, src, capi.FER_JIT_MODE_PERMISSIVE)
+    assert st.code == 0 and b"fused" in res.log
+    kern = C.c_void_p()
+    capi.check("get_kernel", session.call("fer_jit_get_kernel", prog, b"fer_fused_elementwise", None, C.byref(kern)))
+    n = 1000
+    x = synth.normal_f32(51, n, 0.0, 3.0)
+    bx, by = session.alloc(capi.FER_DTYPE_F32, [n]), session.alloc(capi.FER_DTYPE_F32, [n])
+    session.upload(bx, x)
+    vals = (capi.fer_jit_arg_value_t * 3)()
+    vals[0].kind, vals[0].as_.buffer_id = capi.FER_JIT_ARG_BUFFER, bx
+    vals[1].kind, vals[1].as_.buffer_id = capi.FER_JIT_ARG_BUFFER, by
+    vals[2].kind, vals[2].as_.u32 = capi.FER_JIT_ARG_SCALAR_U32, n
+    cfg = capi.fer_jit_launch_cfg_t(4, 1, 1, 256, 1, 1, 0, capi.FER_MEMORY_AUTO)
+    job = C.c_uint64()
+    capi.check("launch", session.call("fer_jit_launch", kern, C.byref(cfg),
+                                      C.byref(capi.fer_jit_arg_pack_t(vals, 3)), C.byref(job)))
+    session.wait(job.value)
+    y = np.empty(n, np.float32)
+    session.download(by, y)
+    r = np.where(x < 0, np.float32(0), x)
+    expect = (1.0 / (1.0 + np.exp(-r.astype(np.float64)))).astype(np.float32)
+    assert np.abs(y - expect).max() < 1e-6
+
+
+def test_custom_allocator_and_regimes(session):
+    """test_c_api_custom_allocator.cpp / regime management."""
+    lib = session.lib
+    log = []
+    torch = pytest.importorskip("torch")
+    keep = {}
+
+    @capi.ALLOC_FN
+    def alloc(nbytes, tier, tag, ctx):
+        t = torch.empty(int(nbytes), dtype=torch.uint8, device="cuda")
+        keep[t.data_ptr()] = t
+        log.append(("alloc", nbytes))
+        return t.data_ptr()
+
+    @capi.FREE_FN
+    def free(p, ctx):
+        log.append(("free", p))
+        keep.pop(p, None)
+
+    ca = capi.fer_custom_allocator_t(alloc, free, None)
+    capi.check("reg", session.call("fer_register_custom_allocator", 77, C.byref(ca)))
+    st = session.call("fer_register_custom_allocator", 1, C.byref(ca))
+    assert st.code == capi.FER_STATUS_INVALID_ARGUMENT
+    ids = (C.c_uint32 * 8)()
+    cnt = C.c_size_t()
+    capi.check("list", session.call("fer_list_registered_regimes", ids, 8, C.byref(cnt)))
+    assert list(ids[:cnt.value]) == [0, 1, 2, 77]
+    bid = session.alloc(capi.FER_DTYPE_F32, [1000], regime=77)
+    assert log and log[0] == ("alloc", 4000)
+    x = np.arange(1000, dtype=np.float32)
+    session.upload(bid, x)
+    y = np.empty_like(x)
+    session.download(bid, y)
+    assert np.array_equal(x, y)
+    session.free(bid)
+    assert log[-1][0] == "free"
+    capi.check("set", session.call("fer_set_default_memory_regime", 77))
+    reg = C.c_uint32()
+    capi.check("get", session.call("fer_get_default_memory_regime", C.byref(reg)))
+    assert reg.value == 77
+    capi.check("unreg", session.call("fer_unregister_custom_allocator", 77))
+    capi.check("get", session.call("fer_get_default_memory_regime", C.byref(reg)))
+    assert reg.value == capi.FER_MEMORY_CUSTOM_POOL
+    st = session.call("fer_unregister_custom_allocator", 77)
+    assert st.code == capi.FER_STATUS_NOT_FOUND
+    del lib
+
+
+def test_external_buffer_with_deleter(session):
+    torch = pytest.importorskip("torch")
+    t = torch.arange(64, dtype=torch.float32, device="cuda")
+    deleted = []
+
+    @capi.DELETER_FN
+    def deleter(p, ctx):
+        deleted.append(p)
+
+    d = capi.desc(capi.FER_DTYPE_F32, [64])
+    bid = C.c_uint64()
+    capi.check("import", session.call("fer_import_external_buffer_with_deleter", C.byref(d), C.c_void_p(t.data_ptr()),
+                                      capi.FER_MEMORY_AUTO, deleter, None, C.byref(bid)))
+    assert session.ptr_of(bid.value) == t.data_ptr()
+    torch.cuda.synchronize()
+    y = np.empty(64, np.float32)
+    session.download(bid.value, y)
+    assert np.array_equal(y, np.arange(64, dtype=np.float32))
+    session.free(bid.value)
+    assert deleted == [t.data_ptr()]
+
+
+def test_stream_handoff_and_jobs(session):
+    torch = pytest.importorskip("torch")
+    s = torch.cuda.Stream()
+    old = session.stream()
+    capi.check("attach", session.call("fer_stream_attach", C.c_uint64(s.cuda_stream)))
+    assert session.stream() == s.cuda_stream
+    n = 1 << 16
+    bx, by = session.alloc(capi.FER_DTYPE_F32, [n]), session.alloc(capi.FER_DTYPE_F32, [n])
+    session.upload(bx, np.ones(n, np.float32))
+    job = session.affine(bx, by, n, 2.0, 1.0, 0)
+    done = C.c_uint8()
+    capi.check("status", session.call("fer_job_status", job, C.byref(done)))
+    session.wait(job)
+    capi.check("status", session.call("fer_job_status", job, C.byref(done)))
+    assert done.value == 1
+    y = np.empty(n, np.float32)
+    session.download(by, y)
+    assert np.all(y == 3.0)
+    capi.check("attach", session.call("fer_stream_attach", C.c_uint64(old)))
+    st = session.call("fer_job_wait", C.c_uint64(10 ** 12))
+    assert st.code == capi.FER_STATUS_NOT_FOUND
+
+
+def test_regimes_cuda_malloc_budget():
+    """CUDA_MALLOC regime honours the per-tier byte budget of the pool config."""
+    with capi.Session(0, pool_bytes=128 << 20, regime=capi.FER_MEMORY_CUDA_MALLOC) as s:
+        b = s.alloc(capi.FER_DTYPE_U8, [32 << 20])
+        with pytest.raises(capi.FerError) as e:
+            s.alloc(capi.FER_DTYPE_U8, [64 << 20])
+        assert e.value.code == capi.FER_STATUS_INTERNAL_ERROR
+        s.free(b)
+        s.free(s.alloc(capi.FER_DTYPE_U8, [60 << 20]))
+
+
+def test_pool_stats_and_raw(session):
+    st0 = capi.fer_pool_stats_t()
+    capi.check("stats", session.call("fer_pool_get_stats", C.byref(st0)))
+    p = C.c_void_p()
+    capi.check("raw", session.call("fer_pool_alloc_raw", C.c_uint64(1000), C.byref(p)))
+    assert p.value % 256 == 0
+    st1 = capi.fer_pool_stats_t()
+    capi.check("stats", session.call("fer_pool_get_stats", C.byref(st1)))
+    assert st1.allocated_bytes == st0.allocated_bytes + 1024
+    capi.check("free", session.call("fer_pool_free_raw", p))
+    st = session.call("fer_pool_free_raw", p)
+    assert st.code == capi.FER_STATUS_NOT_FOUND

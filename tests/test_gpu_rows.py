@@ -1,0 +1,171 @@
+"""Row softmax / layer norm / fused softmax -> layer norm on the GPU through
+the C ABI, against the reference's own kernels (ptx_tensor_softmax_f32 and
+fer::ops::layer_norm applied row by row, oracle/_ref) on the same device
+buffers: bit-exact. Against the CPU oracle: max |diff| / max |ref| <= 1e-5
+(glibc expf and a correctly rounded rsqrt vs CUDA's)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from fercuda_b200 import capi, synth
+from tests import oracle_lib
+
+pytestmark = pytest.mark.gpu
+
+SM, LN = capi.FER_ROWS_SOFTMAX, capi.FER_ROWS_LAYER_NORM
+EPS = 1e-5
+TOL = 1e-5   # max |ours - oracle| / max |oracle|
+
+SHAPES = [(4096, 4096), (64, 4096), (7, 1000), (3, 100), (5, 256), (2, 16384), (2, 20000), (1, 5), (9, 4094),
+          (1, 1), (600, 512)]
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def reference_rows(session, ref, bx, rows, cols, ops):
+    """Reference composition on device: softmax kernel, then one rank-1
+    layer-norm launch per row (as 4096 fer_submit_layer_norm calls would)."""
+    st = C.c_void_p(session.stream())
+    bt = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    bo = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    px, pt, po = session.ptr_of(bx), session.ptr_of(bt), session.ptr_of(bo)
+    src = px
+    if ops & SM:
+        ref.ptx_tensor_softmax_f32(C.c_void_p(px), C.c_void_p(pt if ops & LN else po), rows, cols, st)
+        src = pt
+    if ops & LN:
+        for r in range(rows):
+            ref.refshim_layer_norm_f32(C.c_void_p(src + 4 * r * cols), C.c_void_p(po + 4 * r * cols), cols, EPS, st)
+    out = np.empty((rows, cols), np.float32)
+    session.download(bo, out)
+    session.free(bt)
+    session.free(bo)
+    return out
+
+
+def ours(session, x, ops):
+    rows, cols = x.shape
+    bx = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    by = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    session.upload(bx, x)
+    session.wait(session.rows(bx, by, ops, EPS))
+    y = np.empty_like(x)
+    session.download(by, y)
+    session.free(by)
+    return bx, y
+
+
+@pytest.mark.parametrize("rows,cols", SHAPES)
+@pytest.mark.parametrize("ops", [SM | LN, SM, LN])
+def test_rows_bit_exact_vs_reference(session, rows, cols, ops):
+    ref = oracle_lib.ref_kernels()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    if rows * cols > 1 << 20 and ops != SM | LN:
+        rows = max(1, (1 << 20) // cols)
+    x = synth.normal_f32(1, rows * cols).reshape(rows, cols)
+    bx, y = ours(session, x, ops)
+    y_ref = reference_rows(session, ref, bx, rows, cols, ops)
+    session.free(bx)
+    nan = np.isnan(y) & np.isnan(y_ref)
+    assert np.all((bits(y) == bits(y_ref)) | nan), f"{(bits(y) != bits(y_ref)).sum()} elements differ"
+    assert session.device_errors() == 0
+
+
+def test_rows_vs_cpu_oracle_full_size(session):
+    x = synth.softmax_layernorm_input()
+    rows, cols = x.shape
+    bx, y = ours(session, x, SM | LN)
+    session.free(bx)
+    ref = np.empty_like(x)
+    oracle_lib.load().orc_softmax_layernorm_rows_f32(oracle_lib.ptr(x), oracle_lib.ptr(ref), rows, cols, EPS, 8)
+    err = np.abs(y - ref).max() / np.abs(ref).max()
+    assert err <= TOL
+    # size-independent properties: each row has mean ~0 and variance ~1
+    assert np.abs(y.astype(np.float64).mean(axis=1)).max() < 1e-4
+    assert np.abs(y.astype(np.float64).var(axis=1) - 1.0).max() < 1e-2
+
+
+def test_softmax_vs_float64(session):
+    x = synth.normal_f32(5, 256 * 4096).reshape(256, 4096)
+    bx, y = ours(session, x, SM)
+    session.free(bx)
+    xd = x.astype(np.float64)
+    e = np.exp(xd - xd.max(axis=1, keepdims=True))
+    p = e / e.sum(axis=1, keepdims=True)
+    assert (np.abs(y - p) / p).max() < 1e-5
+    assert np.abs(y.astype(np.float64).sum(axis=1) - 1.0).max() < 1e-5
+
+
+def test_rows_deterministic_10_runs(session):
+    x = synth.softmax_layernorm_input()
+    rows, cols = x.shape
+    bx = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    by = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    session.upload(bx, x)
+    first = None
+    for _ in range(10):
+        session.wait(session.rows(bx, by, SM | LN, EPS))
+        y = np.empty_like(x)
+        session.download(by, y)
+        if first is None:
+            first = y
+        assert np.array_equal(bits(y), bits(first))
+    session.free(bx)
+    session.free(by)
+
+
+def test_gamma_beta(session):
+    rows, cols = 33, 4096
+    x = synth.normal_f32(7, rows * cols).reshape(rows, cols)
+    g = synth.normal_f32(8, cols, 1.0, 0.1)
+    b = synth.normal_f32(9, cols, 0.0, 0.1)
+    bx, by, bg, bb, b0 = (session.alloc(capi.FER_DTYPE_F32, s) for s in ([rows, cols], [rows, cols], [cols], [cols],
+                                                                          [rows, cols]))
+    session.upload(bx, x)
+    session.upload(bg, g)
+    session.upload(bb, b)
+    session.wait(session.rows(bx, by, SM | LN, EPS, gamma=bg, beta=bb))
+    session.wait(session.rows(bx, b0, SM | LN, EPS))
+    y, y0 = np.empty_like(x), np.empty_like(x)
+    session.download(by, y)
+    session.download(b0, y0)
+    assert np.array_equal(bits(y), bits((y0 * g + b).astype(np.float32)))
+
+
+def test_reference_layer_norm_golden(session):
+    """tests/c_api/test_c_api_bridge.cpp:131-171 of the reference: LN of
+    {1,2,3,4}, eps 1e-6, against the host formula within 1e-5."""
+    bx, by = session.alloc(capi.FER_DTYPE_F32, [4]), session.alloc(capi.FER_DTYPE_F32, [4])
+    x = np.array([1, 2, 3, 4], np.float32)
+    session.upload(bx, x)
+    req = capi.fer_layer_norm_request_t(bx, by, 1e-6, capi.FER_MEMORY_AUTO)
+    job = C.c_uint64()
+    capi.check("ln", session.call("fer_submit_layer_norm", C.byref(req), C.byref(job)))
+    session.wait(job.value)
+    y = np.empty(4, np.float32)
+    session.download(by, y)
+    mean = x.mean()
+    ref = (x - mean) / np.sqrt(((x - mean) ** 2).mean() + 1e-6)
+    assert np.abs(y - ref).max() <= 1e-5
+
+
+def test_native_softmax_launcher_bit_exact(session):
+    ref = oracle_lib.ref_kernels()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    rows, cols = 300, 1024
+    x = synth.normal_f32(3, rows * cols, 0.0, 3.0).reshape(rows, cols)
+    bx, b1, b2 = (session.alloc(capi.FER_DTYPE_F32, [rows, cols]) for _ in range(3))
+    session.upload(bx, x)
+    st = C.c_void_p(session.stream())
+    capi.kernels().ptx_tensor_softmax_f32(C.c_void_p(session.ptr_of(bx)), C.c_void_p(session.ptr_of(b1)), rows,
+                                          cols, st)
+    ref.ptx_tensor_softmax_f32(C.c_void_p(session.ptr_of(bx)), C.c_void_p(session.ptr_of(b2)), rows, cols, st)
+    y1, y2 = np.empty_like(x), np.empty_like(x)
+    session.download(b1, y1)
+    session.download(b2, y2)
+    assert np.array_equal(bits(y1), bits(y2))
