@@ -261,6 +261,7 @@ CAPI_PROTOTYPES = {
     # include/fercuda/b200/ext.h
     "fer_submit_rows": (S, [P, C.POINTER(fer_rows_request_t), pu64]),
     "fer_jit_run_chain_f32": (S, [P, C.POINTER(fer_chain_op_t), u32, pu64, u32, u64, pu64]),
+    "fer_submit_gemm": (S, [P, C.POINTER(fer_gemm_request_t), pu64]),
     "fer_session_device_errors": (S, [P, pu32, u8]),
     "fer_pool_get_stats": (S, [P, C.POINTER(fer_pool_stats_t)]),
     "fer_pool_alloc_raw": (S, [P, u64, C.POINTER(P)]),

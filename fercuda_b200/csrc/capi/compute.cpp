@@ -143,4 +143,37 @@ fer_status_t fer_submit_rows(fer_session_t* session, const fer_rows_request_t* r
     return st;
 }
 
+fer_status_t fer_submit_gemm(fer_session_t* session, const fer_gemm_request_t* req, uint64_t* out_job_id) {
+    if (!session) return invalid("session is null");
+    if (!req) return invalid("request is null");
+    Session& S = session->impl;
+    const Buffer* a = S.find(req->a);
+    const Buffer* b = S.find(req->b);
+    const Buffer* o = S.find(req->out);
+    if (!a || !b || !o) return not_found("buffer id not found");
+    if (a->desc.dtype != FER_DTYPE_BF16 || b->desc.dtype != FER_DTYPE_BF16)
+        return invalid("gemm requires bf16 operands");
+    if (o->desc.dtype != FER_DTYPE_F32 && o->desc.dtype != FER_DTYPE_BF16) return invalid("gemm output must be f32 or bf16");
+    if (a->desc.rank != 2 || b->desc.rank != 2 || o->desc.rank != 2) return invalid("gemm requires rank-2 buffers");
+    if (b->desc.dims[0] != a->desc.dims[1] || o->desc.dims[0] != a->desc.dims[0] || o->desc.dims[1] != b->desc.dims[1])
+        return invalid("gemm shape mismatch");
+    if (req->flags != 0) return invalid("gemm flags must be 0");
+    const int M = static_cast<int>(a->desc.dims[0]), K = static_cast<int>(a->desc.dims[1]);
+    const int N = static_cast<int>(b->desc.dims[1]);
+    cudaError_t e;
+    if (K % 8 == 0 && N % 8 == 0) {
+        e = fer_gemm_bf16_tc(a->ptr, b->ptr, o->ptr, M, N, K, o->desc.dtype, S.dev_err, S.stream);
+    } else if (o->desc.dtype == FER_DTYPE_BF16) {
+        e = fer_matmul_ref_order(a->ptr, b->ptr, o->ptr, M, K, N, FER_DTYPE_BF16, S.stream);
+    } else {
+        e = fer_matmul_bf16_f32_ref_order(a->ptr, b->ptr, static_cast<float*>(o->ptr), M, K, N, S.stream);
+    }
+    fer_status_t st = launched(e);
+    if (st.code != FER_STATUS_OK) return st;
+    uint64_t job = 0;
+    st = S.make_job({}, &job);
+    if (st.code == FER_STATUS_OK && out_job_id) *out_job_id = job;
+    return st;
+}
+
 }  // extern "C"

@@ -122,6 +122,8 @@ cudaError_t fer_matmul_ref_order(const void* a, const void* b, void* c, int M, i
                                  cudaStream_t stream);
 cudaError_t fer_cast_to_f32(const void* in, float* out, size_t n, uint32_t dtype, cudaStream_t stream);
 cudaError_t fer_cast_from_f32(const float* in, void* out, size_t n, uint32_t dtype, cudaStream_t stream);
+cudaError_t fer_matmul_bf16_f32_ref_order(const void* a, const void* b, float* c, int M, int K, int N,
+                                          cudaStream_t stream);
 cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K, uint32_t out_dtype,
                              uint32_t* err, cudaStream_t stream);
 }

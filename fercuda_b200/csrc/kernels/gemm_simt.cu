@@ -60,10 +60,10 @@ template <> struct Elem<kU8> {
 constexpr int BM = 128, BN = 128, BK = 16, TM = 8, TN = 8;
 constexpr int kThreads = (BM / TM) * (BN / TN);  // 256
 
-template <uint32_t DT>
+template <uint32_t DT, uint32_t DT_OUT = DT>
 __global__ void __launch_bounds__(kThreads) matmul_ref_order(const typename Elem<DT>::T* __restrict__ A,
                                                              const typename Elem<DT>::T* __restrict__ B,
-                                                             typename Elem<DT>::T* __restrict__ C, int M, int K,
+                                                             typename Elem<DT_OUT>::T* __restrict__ C, int M, int K,
                                                              int N) {
     __shared__ float As[2][BK][BM];
     __shared__ float Bs[2][BK][BN];
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kThreads) matmul_ref_order(const typename Elem
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
             const int c = col0 + tx + j * (BN / TN);
-            if (c < N) Elem<DT>::store(C, static_cast<size_t>(r) * N + c, acc[i][j]);
+            if (c < N) Elem<DT_OUT>::store(C, static_cast<size_t>(r) * N + c, acc[i][j]);
         }
     }
 }
@@ -172,6 +172,17 @@ extern "C" cudaError_t fer_matmul_ref_order(const void* a, const void* b, void* 
         case kU8: return launch_mm<kU8>(a, b, c, M, K, N, stream);
         default: return cudaErrorInvalidValue;
     }
+}
+
+// bf16 operands, f32 output, same per-output chain (used by fer_submit_gemm
+// for shapes the tensor-core kernel does not take).
+extern "C" cudaError_t fer_matmul_bf16_f32_ref_order(const void* a, const void* b, float* c, int M, int K, int N,
+                                                     cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K < 0) return cudaErrorInvalidValue;
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    matmul_ref_order<kBF16, kF32><<<grid, kThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(a),
+                                                                  static_cast<const __nv_bfloat16*>(b), c, M, K, N);
+    return cudaGetLastError();
 }
 
 extern "C" cudaError_t fer_cast_to_f32(const void* in, float* out, size_t n, uint32_t dtype, cudaStream_t s) {

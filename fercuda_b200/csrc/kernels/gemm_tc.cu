@@ -1,0 +1,374 @@
+// Deterministic bf16 GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// C[M,N] = A[M,K] . B[K,N], A and B row-major bf16, f32 accumulation in
+// tensor memory, C f32 or bf16 (round to nearest even).
+//
+// Replaces the reference's CUDA-core GEMM for bf16 operands
+// (k_matmul_f32, src/runtime/ops_bridge.cu:13-31, reached through the f32
+// cast staging of exec_planner.cu:189-302). Each output tile is produced by
+// one CTA that walks K in a fixed order; there is no split-K and no atomic,
+// so results are bit-identical run to run (they differ from the reference's
+// sequential-FMA chain only by summation order).
+//
+// Structure (one CTA per SM, persistent over 128x256 output tiles):
+//   warp 0      TMA producer: A tile [128 x 64] (K-major) and B tile
+//               [64 x 256] (N-major, as four 64-column boxes), 128-byte
+//               swizzle, into a 4-stage shared-memory ring (48 KiB / stage)
+//   warp 1      allocates all 512 tensor-memory columns (two 128x256 f32
+//               accumulators) and issues tcgen05.mma (M=128, N=256, K=16)
+//               from one thread; tcgen05.commit releases ring slots and
+//               hands finished accumulators to the epilogue
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, convert, store;
+//               runs while the MMA warp fills the other accumulator
+// Tile order: groups of 16 M-blocks, N-blocks inside a group, so a wave of
+// 148 CTAs touches ~16 A row-panels and ~9 B column-panels (fits in L2).
+// Every wait is bounded (about one second); on timeout the kernel records an
+// error bit, stops issuing work, releases tensor memory and returns.
+// No TMA multicast is used anywhere.
+#include "sm100_util.cuh"
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+namespace {
+
+using namespace fer::dev;
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;              // 16 KiB
+constexpr int B_BYTES = BK * BN * 2;              // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;    // 48 KiB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr int kThreads = 192;
+constexpr int GROUP_M = 16;
+constexpr uint32_t TMEM_COLS = 512;
+
+struct Bars {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2),
+// descriptor version 1, base offset 0 (tiles are 1024-byte aligned).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;          // version
+    d |= 2ull << 61;          // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B,
+// A K-major, B N-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                            (static_cast<uint32_t>(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int* mb, int* nb) {
+    const int per_group = GROUP_M * num_n;
+    const int g = t / per_group;
+    const int first_m = g * GROUP_M;
+    const int gm = (num_m - first_m) < GROUP_M ? (num_m - first_m) : GROUP_M;
+    const int r = t - g * per_group;
+    *mb = first_m + r % gm;
+    *nb = r / gm;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C, int M,
+                        int N, int K, int out_bf16, uint32_t* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ Bars bars;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int num_k = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars.full[s], 1);
+            mbar_init(&bars.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars.acc_full[b], 1);
+            mbar_init(&bars.acc_empty[b], 4);   // one arrival per epilogue warp
+        }
+        bars.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(&bars.tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars.tmem_base;
+
+    volatile int* abort_flag = &bars.abort_flag;
+    // Each role loop is run by its whole warp (waits voted across the warp,
+    // issue from lane 0) so every warp reaches the final barrier converged.
+    if (warp == 0) {
+        // ---------------- TMA producer
+        int it = 0;
+        for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+            int mb, nb;
+            tile_coords(t, num_m, num_n, &mb, &nb);
+            for (int kt = 0; kt < num_k; ++kt, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars.empty[s], ph ^ 1u))) {
+                    if (lane == 0) report(err, kErrTimeoutSync);
+                    *abort_flag = 1;
+                    break;
+                }
+                if (lane == 0) {
+                    uint8_t* sa = smem + s * STAGE_BYTES;
+                    uint8_t* sb = sa + A_BYTES;
+                    mbar_arrive_expect_tx(&bars.full[s], STAGE_BYTES);
+                    tma_load_2d(sa, &tmA, kt * BK, mb * BM, &bars.full[s]);
+#pragma unroll
+                    for (int c = 0; c < BN / 64; ++c)
+                        tma_load_2d(sb + c * (BK * 128), &tmB, nb * BN + c * 64, kt * BK, &bars.full[s]);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (lane 0 issues)
+        int it = 0, local = 0;
+        for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++local) {
+            const int buf = local & 1;
+            const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars.acc_empty[buf], acc_ph ^ 1u))) {
+                if (lane == 0) report(err, kErrTimeoutSync);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+            bool ok = true;
+            for (int kt = 0; kt < num_k; ++kt, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars.full[s], ph))) {
+                    if (lane == 0) report(err, kErrTimeoutLoad);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sa = smem_addr(smem + s * STAGE_BYTES);
+                    const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        // A: K-major, +32 bytes per 16 elements of K inside the swizzle atom.
+                        const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
+                        // B: N-major, 16 K-rows of 128 bytes per step; 64-column panels 8 KiB apart.
+                        const uint64_t bd = smem_desc(sb + k * 16 * 128, BK * 128, 1024);
+                        mma_bf16(d, ad, bd, (kt | k) ? 1u : 0u);
+                    }
+                    mma_commit(&bars.empty[s]);   // ring slot free once these MMAs finish
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (lane == 0) mma_commit(&bars.acc_full[buf]);   // accumulator complete
+            __syncwarp();
+        }
+    } else {
+        // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        int local = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+            const int buf = local & 1;
+            const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars.acc_full[buf], acc_ph)) || *abort_flag) {
+                if (lane == 0 && !*abort_flag) report(err, kErrTimeoutMma);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            int mb, nb;
+            tile_coords(t, num_m, num_n, &mb, &nb);
+            const int row = mb * BM + row_in_tile;
+            const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c * 32, r);
+                const int col0 = nb * BN + c * 32;
+                if (row < M && col0 < N) {
+                    if (!out_bf16) {
+                        float* out = static_cast<float*>(C) + static_cast<size_t>(row) * N + col0;
+                        if (col0 + 32 <= N) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(out + j) =
+                                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < N) out[j] = __uint_as_float(r[j]);
+                        }
+                    } else {
+                        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(C) + static_cast<size_t>(row) * N + col0;
+                        if (col0 + 32 <= N) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 8) {
+                                uint4 v;
+                                __nv_bfloat162 p0 = __floats2bfloat162_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                                __nv_bfloat162 p1 = __floats2bfloat162_rn(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                                __nv_bfloat162 p2 = __floats2bfloat162_rn(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
+                                __nv_bfloat162 p3 = __floats2bfloat162_rn(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
+                                std::memcpy(&v.x, &p0, 4);
+                                std::memcpy(&v.y, &p1, 4);
+                                std::memcpy(&v.z, &p2, 4);
+                                std::memcpy(&v.w, &p3, 4);
+                                *reinterpret_cast<uint4*>(out + j) = v;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < N) out[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box [box_rows, 64].
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace
+
+// out_dtype: 0 = f32, 2 = bf16 (fer_buffer_dtype_t codes). Requires K % 8 == 0
+// and N % 8 == 0 (16-byte row pitches for the tensor maps) and 16-byte aligned
+// operands; returns cudaErrorInvalidValue otherwise.
+extern "C" cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K,
+                                        uint32_t out_dtype, uint32_t* err, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || (K % 8) || (N % 8)) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u) return cudaErrorInvalidValue;
+    if (out_dtype != 0 && out_dtype != 2) return cudaErrorInvalidValue;
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, a, static_cast<uint64_t>(M), static_cast<uint64_t>(K), BM) ||
+        !make_map(&mb, b, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK))
+        return cudaErrorInvalidValue;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, c, M, N, K, out_dtype == 2 ? 1 : 0, err);
+    return cudaGetLastError();
+}

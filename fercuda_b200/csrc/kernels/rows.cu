@@ -31,6 +31,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 
 namespace {
 
@@ -75,6 +76,18 @@ struct Scratch {
     float fin[4];
 };
 
+// Shared slots for the single-barrier reductions of the bulk kernel: each
+// reduction of a row has its own slots, and every warp finishes the
+// reduction itself from them (same association order as the reference, so
+// the same bits), which needs one barrier per reduction instead of two. A
+// slot is rewritten only three barriers after its last read.
+struct RowSlots {
+    float warp_max[8];
+    float warp_sum[8];
+    float ln_sum[kThreads];
+    float ln_var[kThreads];
+};
+
 // Block max / sum in the k_softmax_f32 order. All 256 threads call it.
 __device__ __forceinline__ float softmax_block_max(float m, Scratch& sc) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -104,58 +117,91 @@ __device__ __forceinline__ float softmax_block_sum(float s, Scratch& sc) {
     return sc.fin[1];
 }
 
+// --- single-barrier variants (every warp finishes the reduction) -----------
+
+// Warp maximum in one instruction. max is exact and order-independent
+// (a NaN operand yields the other operand, as fmaxf does), so this equals
+// the reference's __shfl_down / fmaxf tree bit for bit.
+__device__ __forceinline__ float warp_max_redux(float v) {
+    float r;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
+}
+
+// k_softmax_f32 order: warp tree, then a tree over the 8 warp results padded
+// to 32 lanes. `abort_in` joins the barrier as a vote (__syncthreads_or).
+__device__ __forceinline__ float sb_softmax_max(float m, float* slot8, int abort_in, int* abort_out) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    m = warp_max_redux(m);
+    if (lane == 0) slot8[wid] = m;
+    *abort_out = __syncthreads_or(abort_in);
+    return warp_max_redux(lane < 8 ? slot8[lane] : -INFINITY);
+}
+
+__device__ __forceinline__ float sb_softmax_sum(float s, float* slot8) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    s = warp_down_sum(s);
+    if (lane == 0) slot8[wid] = s;
+    __syncthreads();
+    float w = lane < 8 ? slot8[lane] : 0.0f;
+    return __shfl_sync(0xffffffffu, warp_down_sum(w), 0);
+}
+
 // Sum of 256 per-thread partials in the order of the reference's
-// `for (s = 128; s > 0; s >>= 1) sdata[t] += sdata[t + s]` tree.
-__device__ __forceinline__ float halving_sum_256(float p, Scratch& sc, int slot) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    sc.part[threadIdx.x] = p;
-    __syncthreads();
-    if (wid == 0) {
-        const float* q = sc.part;
-        // steps s = 128, 64, 32
-        float u = ((q[lane] + q[lane + 128]) + (q[lane + 64] + q[lane + 192])) +
-                  ((q[lane + 32] + q[lane + 160]) + (q[lane + 96] + q[lane + 224]));
-        // steps s = 16 .. 1
-        u = warp_down_sum(u);
-        if (lane == 0) sc.fin[slot] = u;
-    }
-    __syncthreads();
-    return sc.fin[slot];
+// `for (s = 128; s > 0; s >>= 1) sdata[t] += sdata[t + s]` tree: steps
+// s = 128, 64, 32 as one expression per lane, then s = 16 .. 1 as the
+// __shfl_down tree.
+__device__ __forceinline__ float sb_halving_sum(float p, float* slot256, int abort_in, int* abort_out) {
+    const int lane = threadIdx.x & 31;
+    slot256[threadIdx.x] = p;
+    *abort_out = __syncthreads_or(abort_in);
+    const float* q = slot256;
+    float u = ((q[lane] + q[lane + 128]) + (q[lane + 64] + q[lane + 192])) +
+              ((q[lane + 32] + q[lane + 160]) + (q[lane + 96] + q[lane + 224]));
+    return __shfl_sync(0xffffffffu, warp_down_sum(u), 0);
 }
 
-__device__ __forceinline__ float halving_max_256(float p, Scratch& sc, int slot) {
+__device__ __forceinline__ float sb_halving_max(float p, float* slot256, int abort_in, int* abort_out) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    sc.part[threadIdx.x] = p;
-    __syncthreads();
-    if (wid == 0) {
-        const float* q = sc.part;
-        float u = fmaxf(fmaxf(fmaxf(q[lane], q[lane + 128]), fmaxf(q[lane + 64], q[lane + 192])),
-                        fmaxf(fmaxf(q[lane + 32], q[lane + 160]), fmaxf(q[lane + 96], q[lane + 224])));
-        u = warp_down_max(u);
-        if (lane == 0) sc.fin[slot] = u;
-    }
-    __syncthreads();
-    return sc.fin[slot];
+    // max is order-independent: reduce each warp first, then the 8 results.
+    p = warp_max_redux(p);
+    if (lane == 0) slot256[wid] = p;
+    *abort_out = __syncthreads_or(abort_in);
+    return warp_max_redux(lane < 8 ? slot256[lane] : -INFINITY);
 }
 
-template <int VPT>
-__device__ __forceinline__ void process_row(float (&v)[VPT], const RowsArgs& a, Scratch& sc, int cols) {
+// One row held in registers (thread t owns columns t + 256 j). The first
+// barrier of the row carries the load-timeout vote and is also the point
+// after which every thread has finished reading the row's ring buffer; the
+// caller's `after_first_barrier` issues the refill there. Returns false if
+// any thread reported a timeout.
+// FULL: cols == 256 * VPT, so no per-element bounds checks.
+template <int VPT, bool FULL, typename Hook>
+__device__ __forceinline__ bool process_row_sb(float (&v)[VPT], const RowsArgs& a, RowSlots& sl, int cols,
+                                               int timed_out, Hook after_first_barrier) {
     const int t = threadIdx.x;
+    int abort_any = 0;
+    bool first = true;
     if (a.flags & kSoftmax) {
         const bool tree = (a.flags & kSoftmaxTree) != 0;
         float m = tree ? -1e30f : -INFINITY;
 #pragma unroll
         for (int j = 0; j < VPT; ++j)
-            if (t + kThreads * j < cols) m = fmaxf(m, v[j]);
-        const float mx = tree ? halving_max_256(m, sc, 0) : softmax_block_max(m, sc);
+            if (FULL || t + kThreads * j < cols) m = fmaxf(m, v[j]);
+        const float mx = tree ? sb_halving_max(m, sl.ln_var, timed_out, &abort_any)
+                              : sb_softmax_max(m, sl.warp_max, timed_out, &abort_any);
+        if (abort_any) return false;
+        after_first_barrier();
+        first = false;
         float s = 0.0f;
 #pragma unroll
         for (int j = 0; j < VPT; ++j)
-            if (t + kThreads * j < cols) {
+            if (FULL || t + kThreads * j < cols) {
                 v[j] = expf(v[j] - mx);
                 s += v[j];
             }
-        const float sum = tree ? halving_sum_256(s, sc, 1) : softmax_block_sum(s, sc);
+        int dummy = 0;
+        const float sum = tree ? sb_halving_sum(s, sl.ln_sum, 0, &dummy) : sb_softmax_sum(s, sl.warp_sum);
         const float inv = 1.0f / sum;
 #pragma unroll
         for (int j = 0; j < VPT; ++j) v[j] *= inv;
@@ -165,16 +211,24 @@ __device__ __forceinline__ void process_row(float (&v)[VPT], const RowsArgs& a, 
         float s = 0.0f;
 #pragma unroll
         for (int j = 0; j < VPT; ++j)
-            if (t + kThreads * j < cols) s += v[j];
-        const float mean = halving_sum_256(s, sc, 2) / n;
+            if (FULL || t + kThreads * j < cols) s += v[j];
+        // With the tree-order softmax the ln_sum / ln_var slots were used by
+        // its reductions; the barriers in between keep the reuse safe.
+        const float mean = sb_halving_sum(s, (a.flags & kSoftmaxTree) ? sl.ln_var : sl.ln_sum,
+                                          first ? timed_out : 0, &abort_any) / n;
+        if (first) {
+            if (abort_any) return false;
+            after_first_barrier();
+        }
         float q = 0.0f;
 #pragma unroll
         for (int j = 0; j < VPT; ++j)
-            if (t + kThreads * j < cols) {
+            if (FULL || t + kThreads * j < cols) {
                 const float d = v[j] - mean;
                 q += d * d;
             }
-        const float var = halving_sum_256(q, sc, 3) / n;
+        int dummy = 0;
+        const float var = sb_halving_sum(q, (a.flags & kSoftmaxTree) ? sl.ln_sum : sl.ln_var, 0, &dummy) / n;
         const float inv_std = rsqrtf(var + a.eps);
 #pragma unroll
         for (int j = 0; j < VPT; ++j) v[j] = (v[j] - mean) * inv_std;
@@ -182,23 +236,23 @@ __device__ __forceinline__ void process_row(float (&v)[VPT], const RowsArgs& a, 
 #pragma unroll
             for (int j = 0; j < VPT; ++j) {
                 const int c = t + kThreads * j;
-                if (c < cols) {
+                if (FULL || c < cols) {
                     if (a.gamma) v[j] = v[j] * a.gamma[c];
                     if (a.beta) v[j] = v[j] + a.beta[c];
                 }
             }
         }
     }
+    return true;
 }
 
 // Persistent bulk-copy kernel. Requires 256 <= cols <= 256*VPT, cols % 4 == 0,
 // x 16-byte aligned, dynamic shared memory = stages * cols * 4 bytes.
-template <int VPT>
+template <int VPT, bool FULL>
 __global__ void __launch_bounds__(kThreads) rows_bulk_kernel(RowsArgs a) {
     extern __shared__ __align__(128) float ring[];
     __shared__ __align__(8) uint64_t full[kMaxStages];
-    __shared__ Scratch sc;
-    __shared__ int abort_flag;
+    __shared__ RowSlots sl;
 
     const int t = threadIdx.x;
     const int cols = a.cols;
@@ -208,7 +262,6 @@ __global__ void __launch_bounds__(kThreads) rows_bulk_kernel(RowsArgs a) {
                             ? (a.rows - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
                             : 0;
     if (t == 0) {
-        abort_flag = 0;
         for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
     }
@@ -225,34 +278,33 @@ __global__ void __launch_bounds__(kThreads) rows_bulk_kernel(RowsArgs a) {
         const int s = i % stages;
         const uint32_t parity = static_cast<uint32_t>(i / stages) & 1u;
         const size_t r = blockIdx.x + static_cast<size_t>(i) * gridDim.x;
-        if (!mbar_wait(&full[s], parity)) abort_flag = 1;
-        __syncthreads();
-        if (abort_flag) {
-            if (t == 0) report(a.err, kErrTimeoutLoad);
-            return;
-        }
+        const int timed_out = mbar_wait(&full[s], parity) ? 0 : 1;
         float v[VPT];
         const float* buf = ring + static_cast<size_t>(s) * cols;
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
             const int c = t + kThreads * j;
-            v[j] = c < cols ? buf[c] : 0.0f;
+            v[j] = (FULL || c < cols) ? buf[c] : 0.0f;
         }
-        // Every thread has read buffer s once it reaches this barrier; the
-        // refill is issued behind it.
-        __syncthreads();
-        if (t == 0 && i + stages < my_rows) {
-            fence_proxy_async_smem();
-            const size_t rn = r + static_cast<size_t>(stages) * gridDim.x;
-            mbar_arrive_expect_tx(&full[s], row_bytes);
-            bulk_g2s(ring + static_cast<size_t>(s) * cols, a.x + rn * cols, row_bytes, &full[s]);
+        // Refill of ring slot s with the row `stages` ahead, issued once every
+        // thread is past the row's first barrier (all reads of slot s done).
+        auto refill = [&]() {
+            if (t == 0 && i + stages < my_rows) {
+                fence_proxy_async_smem();
+                const size_t rn = r + static_cast<size_t>(stages) * gridDim.x;
+                mbar_arrive_expect_tx(&full[s], row_bytes);
+                bulk_g2s(ring + static_cast<size_t>(s) * cols, a.x + rn * cols, row_bytes, &full[s]);
+            }
+        };
+        if (!process_row_sb<VPT, FULL>(v, a, sl, cols, timed_out, refill)) {
+            if (t == 0) report(a.err, kErrTimeoutLoad);
+            return;
         }
-        process_row<VPT>(v, a, sc, cols);
         float* out = a.y + r * cols;
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
             const int c = t + kThreads * j;
-            if (c < cols) st_global_cs(out + c, v[j]);
+            if (FULL || c < cols) st_global_cs(out + c, v[j]);
         }
     }
 }
@@ -370,26 +422,55 @@ int num_sms() {
     return g_num_sms;
 }
 
-template <int VPT>
+template <int VPT, bool FULL>
 cudaError_t launch_bulk(RowsArgs a, cudaStream_t stream) {
     const size_t row_bytes = static_cast<size_t>(a.cols) * 4;
-    // Ring: as many row buffers as fit in 48 KiB (2..8), so three or more
-    // CTAs share an SM and keep >100 KiB of reads in flight per SM.
-    int stages = static_cast<int>((48u << 10) / row_bytes);
-    if (stages < 2) stages = 2;
-    if (stages > kMaxStages) stages = kMaxStages;
-    a.stages = stages;
-    const size_t smem = row_bytes * stages;
-    cudaError_t e = cudaFuncSetAttribute(rows_bulk_kernel<VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    // Ring depth: the deepest ring among those that keep the most CTAs
+    // resident per SM (2..8 row buffers). FERCUDA_ROWS_STAGES overrides it.
+    static int override_stages = -1;
+    if (override_stages < 0) {
+        const char* e = std::getenv("FERCUDA_ROWS_STAGES");
+        override_stages = e ? std::atoi(e) : 0;
+    }
+    // Decision cache per (device, cols) for this instantiation.
+    struct Choice { int dev, cols, stages, per_sm; };
+    static Choice cache[8] = {};
+    static int cache_n = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (int k = 0; k < cache_n; ++k)
+        if (cache[k].dev == dev && cache[k].cols == a.cols) {
+            a.stages = cache[k].stages;
+            int grid = num_sms() * cache[k].per_sm;
+            if (grid > a.rows) grid = a.rows;
+            rows_bulk_kernel<VPT, FULL><<<grid, kThreads, row_bytes * a.stages, stream>>>(a);
+            return cudaGetLastError();
+        }
+    // The attribute is only an upper bound; occupancy follows the smem each
+    // launch passes, so it is set once to the largest ring used.
+    cudaError_t e = cudaFuncSetAttribute(rows_bulk_kernel<VPT, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(200u << 10));
     if (e != cudaSuccess) return e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_bulk_kernel<VPT>, kThreads, smem);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) per_sm = 1;
-    int grid = num_sms() * per_sm;
+    int best_stages = 2, best_per_sm = 0;
+    for (int st = kMaxStages; st >= 2; --st) {
+        if (override_stages >= 2 && st != override_stages) continue;
+        const size_t smem = row_bytes * st;
+        if (smem > (200u << 10)) continue;
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_bulk_kernel<VPT, FULL>, kThreads, smem);
+        if (e != cudaSuccess) return e;
+        if (per_sm > best_per_sm) {
+            best_per_sm = per_sm;
+            best_stages = st;
+        }
+    }
+    if (best_per_sm < 1) best_per_sm = 1;
+    a.stages = best_stages;
+    const size_t smem = row_bytes * best_stages;
+    if (cache_n < 8) cache[cache_n++] = Choice{dev, a.cols, best_stages, best_per_sm};
+    int grid = num_sms() * best_per_sm;
     if (grid > a.rows) grid = a.rows;
-    rows_bulk_kernel<VPT><<<grid, kThreads, smem, stream>>>(a);
+    rows_bulk_kernel<VPT, FULL><<<grid, kThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -405,12 +486,25 @@ extern "C" cudaError_t fer_rows_f32(const float* x, float* y, const float* gamma
                          (reinterpret_cast<uintptr_t>(x) % 16) == 0 && x != y;
     if (bulk_ok) {
         const int vpt = (cols + kThreads - 1) / kThreads;
-        if (vpt <= 2) return launch_bulk<2>(a, stream);
-        if (vpt <= 4) return launch_bulk<4>(a, stream);
-        if (vpt <= 8) return launch_bulk<8>(a, stream);
-        if (vpt <= 16) return launch_bulk<16>(a, stream);
-        if (vpt <= 32) return launch_bulk<32>(a, stream);
-        return launch_bulk<64>(a, stream);
+        const bool full = cols % kThreads == 0;
+        if (full) {
+            switch (vpt) {
+                case 1: return launch_bulk<1, true>(a, stream);
+                case 2: return launch_bulk<2, true>(a, stream);
+                case 4: return launch_bulk<4, true>(a, stream);
+                case 8: return launch_bulk<8, true>(a, stream);
+                case 16: return launch_bulk<16, true>(a, stream);
+                case 32: return launch_bulk<32, true>(a, stream);
+                case 64: return launch_bulk<64, true>(a, stream);
+                default: break;
+            }
+        }
+        if (vpt <= 2) return launch_bulk<2, false>(a, stream);
+        if (vpt <= 4) return launch_bulk<4, false>(a, stream);
+        if (vpt <= 8) return launch_bulk<8, false>(a, stream);
+        if (vpt <= 16) return launch_bulk<16, false>(a, stream);
+        if (vpt <= 32) return launch_bulk<32, false>(a, stream);
+        return launch_bulk<64, false>(a, stream);
     }
     int grid = rows < num_sms() * 8 ? rows : num_sms() * 8;
     rows_generic_kernel<<<grid, kThreads, 0, stream>>>(a);

@@ -50,15 +50,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `ns`
+// nanoseconds while the phase is incomplete.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete; false after about
-// one second (the caller reports the error and stops).
+// one second (the caller reports the error and stops). Threads sleep in
+// try_wait between polls and read the clock only every 64 polls, so waiting
+// warps take almost no issue slots from working ones.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) return false;
+    for (uint32_t k = 1;; ++k) {
+        if (mbar_try_wait_sleep(bar, parity, 2000)) return true;
+        if ((k & 63u) == 0 && clock64() - t0 > kWaitCycles) return false;
     }
-    return true;
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.

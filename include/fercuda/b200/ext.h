@@ -83,6 +83,22 @@ fer_status_t fer_jit_run_chain_f32(fer_session_t* session, const fer_chain_op_t*
                                    const uint64_t* inputs, uint32_t n_inputs, uint64_t output,
                                    uint64_t* out_job_id);
 
+/* ---- deterministic tensor-core GEMM ---------------------------------------
+ * out[M,N] = a[M,K] . b[K,N], bf16 operands, f32 accumulation in tensor
+ * memory (tcgen05), fixed K order, no split-K: bit-identical run to run.
+ * out dtype f32 or bf16 (round to nearest even). Row-major buffers; K and N
+ * multiples of 8. Other shapes take the CUDA-core kernel with the reference's
+ * sequential accumulation order (also deterministic). */
+typedef struct fer_gemm_request {
+    uint64_t a;
+    uint64_t b;
+    uint64_t out;
+    uint32_t flags;          /* reserved, 0 */
+    uint32_t memory_regime;
+} fer_gemm_request_t;
+
+fer_status_t fer_submit_gemm(fer_session_t* session, const fer_gemm_request_t* req, uint64_t* out_job_id);
+
 /* ---- diagnostics ------------------------------------------------------------ */
 
 /* Error bits that kernels of this session reported (bounded waits that ran

@@ -197,15 +197,21 @@ def test_jit_exec_add_scalar(session):
 
 def test_jit_lowering_contracts(session):
     """test_c_api_jit_lowering.cpp: impossible SM rejected; fusion notes in log.
-    Here the fused kernel the lowering generates is also compiled and run."""
-    st, _, _ = _jit_compile(session, '// fercuda:require_sm>=99\nextern "C" __global__ void k(float* x){}\n')
-    if st.code == 0:
-        pytest.skip("device reports sm >= 99")
+    (The reference test asks for sm >= 99, which a B200, sm_100, satisfies; the
+    rejection is checked with 999.) Here the fused kernel the lowering
+    generates is also compiled and run."""
+    st, _, _ = _jit_compile(session, '// fercuda:require_sm>=999\nextern "C" __global__ void k(float* x){}\n')
+    assert st.code == capi.FER_STATUS_INVALID_ARGUMENT
+    st, prog, _ = _jit_compile(session, '// fercuda:require_sm>=99\nextern "C" __global__ void k(float* x){}\n')
+    assert st.code == capi.FER_STATUS_OK
     src = ("// fercuda:fuse=elementwise_chain\n// fercuda:ir_node=elementwise_relu\n"
            "// fercuda:ir_node=elementwise_sigmoid\n"
            'extern "C" __global__ void k(float* x){ if(threadIdx.x==0) x[0]+=1.0f; }\n')
     st, prog, res = _jit_compile(session, src, capi.FER_JIT_MODE_PERMISSIVE)
     assert st.code == 0 and b"fused" in res.log
+    session.call("fer_jit_release_program", prog)
+    st, prog, res = _jit_compile(session, src, capi.FER_JIT_MODE_PERMISSIVE)
+    assert st.code == 0 and res.cache_hit == 1
     kern = C.c_void_p()
     capi.check("get_kernel", session.call("fer_jit_get_kernel", prog, b"fer_fused_elementwise", None, C.byref(kern)))
     n = 1000

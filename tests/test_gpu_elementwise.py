@@ -2,8 +2,9 @@
   (a) the reference's own kernels (oracle/_ref, built from the reference
       sources with the reference's flags) run on the same device buffers:
       bit-exact;
-  (b) the CPU oracle: bit-exact except sigmoid's expf (CUDA vs glibc), so
-      within 2 ULP;
+  (b) the CPU oracle: bit-exact except sigmoid's expf (CUDA's <= 2 ULP vs
+      glibc's <= 1 ULP, carried through 1+e, the division and the product),
+      so within 4 ULP;
 plus run-to-run determinism and the reference's own affine-intent test."""
 import ctypes as C
 
@@ -91,7 +92,8 @@ def test_chain_vs_cpu_oracle_full_size(session):
     ref = np.empty(n, np.float32)
     oracle_lib.load().orc_chain_f32(oracle_lib.ptr(x), oracle_lib.ptr(ref), n, A, B, 8)
     ulp = np.abs(bits(y).astype(np.int64) - bits(ref).astype(np.int64))
-    assert ulp.max() <= 2
+    assert ulp.max() <= 4
+    assert (ulp == 0).mean() > 0.9
     # affine + relu stage is exact: where relu clamps, the product is exactly 0
     assert np.all(y[(x * np.float32(A) + np.float32(B)) <= 0] == 0)
 
@@ -163,7 +165,7 @@ def test_native_launchers_vs_reference_unaligned(session):
             y1, y2 = np.empty(n + 1, np.float32), np.empty(n + 1, np.float32)
             session.download(b1, y1)
             session.download(b2, y2)
-            assert same_bits(y1[off:], y2[off:]), (name, off)
+            assert same_bits(y1[off:off + m], y2[off:off + m]), (name, off)
 
 
 def test_reference_affine_intent_golden(session):

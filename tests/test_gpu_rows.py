@@ -84,9 +84,15 @@ def test_rows_vs_cpu_oracle_full_size(session):
     oracle_lib.load().orc_softmax_layernorm_rows_f32(oracle_lib.ptr(x), oracle_lib.ptr(ref), rows, cols, EPS, 8)
     err = np.abs(y - ref).max() / np.abs(ref).max()
     assert err <= TOL
-    # size-independent properties: each row has mean ~0 and variance ~1
+    # size-independent properties: each row has mean ~0 and variance
+    # var_p / (var_p + eps), var_p the variance of the softmax row (eps
+    # dominates here: softmax outputs of 4096 columns are ~1/4096)
+    xd = x.astype(np.float64)
+    e = np.exp(xd - xd.max(axis=1, keepdims=True))
+    p = e / e.sum(axis=1, keepdims=True)
+    vp = p.var(axis=1)
     assert np.abs(y.astype(np.float64).mean(axis=1)).max() < 1e-4
-    assert np.abs(y.astype(np.float64).var(axis=1) - 1.0).max() < 1e-2
+    assert np.abs(y.astype(np.float64).var(axis=1) / (vp / (vp + EPS)) - 1.0).max() < 1e-3
 
 
 def test_softmax_vs_float64(session):
