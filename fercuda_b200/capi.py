@@ -326,6 +326,7 @@ KERNEL_PROTOTYPES = {
     "ptx_tensor_softmax_f32": (None, [P, P, sz, sz, P]),
     "ptx_tensor_softmax_layer_norm_f32": (None, [P, P, P, P, sz, sz, f32, P]),
     "ptx_tensor_layer_norm_rows_f32": (None, [P, P, P, P, sz, sz, f32, P]),
+    "ptx_tensor_reduce_f32_noalloc": (C.c_int, [P, P, sz, C.c_int, P]),
 }
 
 _LIBS: dict[str, C.CDLL] = {}

@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 namespace {
 
@@ -122,4 +123,64 @@ extern "C" cudaError_t fer_conv2d_f32(const float* input, const float* weights, 
     conv2d_direct<<<(total + 255) / 256, 256, 0, s>>>(input, weights, bias, output, H, W, C, KH, KW, F, pad_h, pad_w,
                                                       sh, sw, relu);
     return cudaGetLastError();
+}
+
+// ---- reduction into caller-provided memory only ------------------------------
+// Some callers cannot allocate device memory at the moment they need a
+// reduction:
+//   - a custom allocator callback registered with fer_register_custom_allocator
+//     (or any code inside an allocator) would re-enter the allocator it is
+//     part of;
+//   - a process whose cudaMalloc is interposed and routed into the pool being
+//     managed cannot allocate from inside that pool's own bookkeeping;
+//   - a process that has reserved nearly all device memory for its pools at
+//     start-up may have nothing left for cudaMalloc to return.
+// ptx_tensor_reduce_f32_noalloc serves them: the per-CTA partials live in the
+// fixed device array below, which every GPU that loads this library holds
+// until the process exits, so the call itself allocates nothing.
+//   - At most kNoAllocMaxPartials partials, i.e. n <= 33,554,432 elements;
+//     larger n is rejected with cudaErrorInvalidValue before any launch.
+//   - All calls share the array. Each call overwrites every partial it reads
+//     before reading it, so nothing needs clearing between calls; calls that
+//     overlap on the GPU (different streams, or several host threads) race
+//     on the array and must be serialised by the caller.
+//   - The first call on a device looks the array's device address up with
+//     cudaGetSymbolAddress (this device current). Make that first call before
+//     any stream capture begins.
+constexpr unsigned kNoAllocMaxPartials = 65536;   // 256 KiB of f32 partials
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocMaxPartials];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[64] = {};
+
+// Device address of g_noalloc_partials for the current device. In host code
+// the symbol itself is only a host-side stand-in, so kernels get this address.
+cudaError_t noalloc_partials(float** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        if (e != cudaSuccess) return e;
+        g_noalloc_addr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" cudaError_t ptx_tensor_reduce_f32_noalloc(const float* in, float* out, size_t n, int is_max,
+                                                     cudaStream_t stream) {
+    if (!in || !out || n == 0) return cudaErrorInvalidValue;
+    if (n > static_cast<size_t>(kNoAllocMaxPartials) * 2u * kBlock) return cudaErrorInvalidValue;
+    float* partials = nullptr;
+    const cudaError_t e = noalloc_partials(&partials);
+    if (e != cudaSuccess) return e;
+    return fer_reduce_f32(in, out, partials, static_cast<unsigned int>(n), is_max, stream);
 }

@@ -36,6 +36,23 @@ void ptx_tensor_softmax_layer_norm_f32(float* in, float* out, const float* gamma
 void ptx_tensor_layer_norm_rows_f32(float* in, float* out, const float* gamma, const float* beta,
                                     size_t rows, size_t cols, float eps, cudaStream_t stream);
 
+/* No counterpart in the reference. Sum (is_max = 0: out[0] += sum(in)) or
+ * maximum (is_max != 0: out[0] = max(out[0], max(in))) of n f32 values, the
+ * same deterministic two-stage reduction as the REDUCE_SUM / REDUCE_MAX JIT
+ * intents, for callers that cannot allocate device memory at that moment
+ * (allocator callbacks, processes whose cudaMalloc is routed into the pool
+ * being managed, processes that reserved all device memory up front). The
+ * scratch is a fixed device array inside this library (held by every GPU
+ * that loads it until exit); the call allocates nothing.
+ *   - n <= PTX_REDUCE_NOALLOC_MAX_ELEMENTS, else cudaErrorInvalidValue and no
+ *     launch;
+ *   - calls share the scratch: calls that overlap on the GPU race, so
+ *     serialise them;
+ *   - the first call on a device resolves the scratch address; make it
+ *     before any stream capture begins. */
+#define PTX_REDUCE_NOALLOC_MAX_ELEMENTS 33554432u
+cudaError_t ptx_tensor_reduce_f32_noalloc(const float* in, float* out, size_t n, int is_max, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
