@@ -1,32 +1,34 @@
-"""Benchmark of the hot path, one JSON line on rank 0.
+"""Benchmark of the hot path; rank 0 prints one JSON line.
 
-Default workload (N = 1): row softmax followed by layer norm (gamma 1, beta 0,
-eps 1e-5) over f32 [4096, 4096], entries N(0,1) from seed 1 - one step is one
-fused pass over the whole batch through fer_submit_rows. For N > 1 every rank
-runs the same workload on its own GPU (replicas, weak scaling); `value` sums
-all ranks' bytes over the slowest rank's time.
+Default workload: the decoder-only transformer forward (8 layers, d 1024,
+16 heads, ffn 4096, vocab 32000, seq 512, global batch 64; bf16 weights
+N(0, 0.02) from seed 4, tokens uniform from seed 5), batch-sharded over the
+N GPUs of the launch (one process per GPU), weights initialised on rank 0 and
+broadcast once over NCCL, no collective inside a forward. One step is one
+forward of the whole global batch; `value` is global tokens per second over
+the slowest rank's device time (strong scaling: the batch is fixed).
 
-  value    algorithmic HBM bytes (read x + write y = 8 B/element) per second,
-           device-timed with CUDA events over exactly K steps, inputs resident;
-           L2 is defeated by rotating over 3 input/output pairs (384 MiB > L2)
-  e2e      the same bytes per second through the C ABI with host buffers:
-           fer_upload_bytes (pinned) + fer_submit_rows + fer_download_bytes
-  roofline achieved GB/s of the fused row kernel (per-launch CUDA events)
-           against the measured HBM copy bandwidth of MEASURED_PEAKS.json
-  cpu_baseline the oracle (CPU restatement, C, all host threads) on the same
-           workload
+Other workloads (--workload), each also reported under `subresults` of the
+default run on one GPU:
+  softmax_layernorm  row softmax -> layer norm over f32 [4096, 4096]      HBM GB/s
+  fused_elementwise  relu(1.5x - 0.25) * sigmoid(x), f32 2^20             HBM GB/s
+  gemm               bf16 8192^3 -> f32, deterministic tcgen05 GEMM       TFLOP/s
+  tlsf               1M-op alloc/free trace (256 B - 16 MiB, 60/40, live <= 64 GiB),
+                     each allocation filled by a kernel; alloc latency   ns (p50)
 
---impl reference runs the reference's CPU implementation of the path (the
-oracle port) with all host threads on the same config instead.
---workload fused_elementwise measures y = relu(1.5x - 0.25) * sigmoid(x) over
-2^20 f32 through fer_tensor_run_affine_f32 the same way.
+Timing: CUDA events on the session stream over exactly K steps after W
+warm-up steps, barrier + synchronize on both sides, max over ranks.
+`e2e` repeats the step through the public C ABI with pinned host buffers
+(inputs uploaded and results downloaded inside the timed region).
+`--impl reference` times the reference's CPU implementation of the path: the
+oracle port (oracle/), all host threads, rank 0 only.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes as C
+import datetime
 import json
-import math
 import os
 import re
 import subprocess
@@ -40,15 +42,18 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-HBM_FALLBACK_GBS = 6650.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC_HBM = "HBM GB/s (fused elementwise, softmax)"
+METRIC_TOK = "transformer fwd tokens/s"
 
 
-def peaks():
+def peak(key: str):
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d.get("hbm_gbs", HBM_FALLBACK_GBS)), "measured"
-    return HBM_FALLBACK_GBS, "fallback"
+        if key in d:
+            return float(d[key]), "measured"
+    return FALLBACK[key], "fallback"
 
 
 def profiled_traffic(name: str):
@@ -61,14 +66,18 @@ def profiled_traffic(name: str):
     return int(m.group(1)) if m else None
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 50 ms."""
 
     def __init__(self, index: int):
-        self.index = index
-        self.samples = []
-        self.proc = None
-        self.t0 = self.t1 = None
+        self.index, self.samples, self.proc, self.t0, self.t1 = index, [], None, None, None
 
     def start(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -81,8 +90,7 @@ class ClockSampler:
         except (OSError, FileNotFoundError):
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
+        threading.Thread(target=self._read, daemon=True).start()
 
     def _read(self):
         for line in self.proc.stdout:
@@ -103,25 +111,26 @@ class ClockSampler:
             self.proc.wait(timeout=2)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        lo, hi = (self.t0 or 0) - 0.1, (self.t1 or time.time()) + 0.1
+        lo, hi = (self.t0 or 0) - 0.06, (self.t1 or time.time()) + 0.06
         sel = [s for t, s in self.samples if lo <= t <= hi] or [s for _, s in self.samples[-3:]]
-        sm = [float(s[1]) for s in sel if len(s) > 8 and s[1].replace(".", "").isdigit()]
-        smax = [float(s[2]) for s in sel if len(s) > 8 and s[2].replace(".", "").isdigit()]
+        num = lambda v: v.replace(".", "", 1).isdigit()
+        sm = [float(s[1]) for s in sel if len(s) > 8 and num(s[1])]
+        smax = [float(s[2]) for s in sel if len(s) > 8 and num(s[2])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for s in sel if len(s) > 8 for i in range(4) if s[5 + i] == "Active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
                 "reasons": reasons, "samples": len(sel)}
 
 
-# ------------------------------------------------------------------ workloads
+# ================================================================ workloads
 
-class RowsWorkload:
-    name = "softmax_layernorm"
-    kernel = "rows_softmax_layernorm_4096x4096"
+
+class Rows:
+    """Row softmax -> layer norm, f32 [4096, 4096] (fer_submit_rows)."""
+    metric, unit, kernel = METRIC_HBM, "GB/s", "rows_softmax_layernorm_4096x4096"
 
     def __init__(self, s, capi, synth, rows=4096, cols=4096):
-        self.s, self.capi = s, capi
-        self.rows, self.cols = rows, cols
+        self.s, self.capi, self.rows, self.cols = s, capi, rows, cols
         self.eps = synth.SOFTMAX_LAYERNORM["eps"]
         self.x = synth.softmax_layernorm_input(rows, cols)
         self.pairs = []
@@ -132,37 +141,63 @@ class RowsWorkload:
         self.req = [capi.fer_rows_request_t(bx, by, 0, 0, self.eps, capi.FER_ROWS_SOFTMAX | capi.FER_ROWS_LAYER_NORM,
                                             capi.FER_MEMORY_AUTO) for bx, by in self.pairs]
         self.job = C.c_uint64()
-        self.bytes_per_step = 8 * rows * cols
+        self.units_per_step = 8 * rows * cols           # algorithmic bytes
+        self.launches_per_step = 1
         self.h2d = self.d2h = 4 * rows * cols
+        self.hx = self.hy = None
 
     def step(self, i):
         st = self.s.call("fer_submit_rows", C.byref(self.req[i % 3]), C.byref(self.job))
         if st.code:
             raise RuntimeError(st.message)
 
-    def config(self):
-        return {"workload": f"softmax_layernorm_{self.rows}x{self.cols}_f32", "rows": self.rows, "cols": self.cols,
-                "eps": self.eps, "gamma": 1.0, "beta": 0.0, "input": "N(0,1) seed 1",
-                "l2": "rotating 3 input/output pairs (384 MiB > 126 MB L2)", "api": "fer_submit_rows"}
+    def config(self, world):
+        return self.describe(world)
 
-    def e2e_step(self, hx, hy):
+    @staticmethod
+    def describe(world, rows=4096, cols=4096):
+        return {"workload": f"softmax_layernorm_{rows}x{cols}_f32", "rows": rows, "cols": cols,
+                "eps": 1e-5, "gamma": 1.0, "beta": 0.0, "input": "N(0,1) seed 1",
+                "l2": "rotating 3 input/output pairs (384 MiB > 126 MB L2)", "api": "fer_submit_rows",
+                "parallelism": f"replicas x{world}"}
+
+    def e2e_prepare(self, torch):
+        self.hx = torch.from_numpy(self.x.reshape(-1)).pin_memory().numpy()
+        self.hy = torch.empty(self.hx.size, dtype=torch.float32).pin_memory().numpy()
+
+    def e2e_step(self):
         bx, by = self.pairs[0]
-        self.s.upload(bx, hx)
+        self.s.upload(bx, self.hx)
         self.step(0)
-        self.s.download(by, hy)
+        self.s.download(by, self.hy)
 
-    def cpu(self, orc, threads, reps=3):
-        y = np.empty_like(self.x)
+    def roofline(self, kern_ms):
+        pk, src = peak("hbm_gbs")
+        ach = self.units_per_step / (kern_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(ach, 1), "peak": pk, "unit": "GB/s", "frac": round(ach / pk, 4),
+                "traffic": profiled_traffic(self.kernel), "algorithmic_bytes_per_launch": self.units_per_step,
+                "peak_source": pk and src, "kernel": "rows_bulk_kernel", "kernel_ms_median": round(kern_ms, 5)}
+
+    @staticmethod
+    def cpu(threads, reps=3):
+        from fercuda_b200 import synth
+        from tests import oracle_lib
+
+        x = synth.softmax_layernorm_input()
+        y = np.empty_like(x)
+        orc = oracle_lib.load()
+        fn = lambda: orc.orc_softmax_layernorm_rows_f32(x.ctypes.data_as(C.c_void_p), y.ctypes.data_as(C.c_void_p),
+                                                        x.shape[0], x.shape[1], C.c_float(1e-5), threads)
+        fn()
         t0 = time.perf_counter()
         for _ in range(reps):
-            orc.orc_softmax_layernorm_rows_f32(self.x.ctypes.data_as(C.c_void_p), y.ctypes.data_as(C.c_void_p),
-                                               self.rows, self.cols, C.c_float(self.eps), threads)
+            fn()
         dt = (time.perf_counter() - t0) / reps
-        return self.bytes_per_step / dt / 1e9, f"full {self.rows}x{self.cols} batch x{reps}"
+        return 8 * x.size / dt / 1e9, f"full 4096x4096 batch, mean of {reps} passes", threads
 
 
-class ChainWorkload:
-    name = "fused_elementwise"
+class Chain(Rows):
+    """y = relu(1.5x - 0.25) * sigmoid(x), f32 2^20 (fer_tensor_run_affine_f32)."""
     kernel = "fused_chain_2p20"
 
     def __init__(self, s, capi, synth, n=1 << 20):
@@ -178,111 +213,459 @@ class ChainWorkload:
             self.pairs.append((bx, by))
         self.fusion = capi.FER_JIT_INTENT_FUSION_RELU | capi.FER_JIT_INTENT_FUSION_MUL_SIGMOID_INPUT
         self.job = C.c_uint64()
-        self.lib = s.lib
-        self.bytes_per_step = 8 * n
+        self.units_per_step = 8 * n
+        self.launches_per_step = 1
         self.h2d = self.d2h = 4 * n
-        s.wait(s.affine(*self.pairs[0], n, self.a, self.b, self.fusion))   # compile once
+        s.wait(s.affine(*self.pairs[0], n, self.a, self.b, self.fusion))   # NVRTC compile outside timing
 
     def step(self, i):
         bx, by = self.pairs[i % self.nbuf]
-        st = self.lib.fer_tensor_run_affine_f32(self.s.ptr, self.capi.fer_tensor_handle_t(bx),
-                                                self.capi.fer_tensor_handle_t(by), self.n, self.a, self.b,
-                                                self.fusion, 0, self.capi.FER_MEMORY_AUTO, C.byref(self.job))
+        st = self.s.lib.fer_tensor_run_affine_f32(self.s.ptr, self.capi.fer_tensor_handle_t(bx),
+                                                  self.capi.fer_tensor_handle_t(by), self.n, self.a, self.b,
+                                                  self.fusion, 0, self.capi.FER_MEMORY_AUTO, C.byref(self.job))
         if st.code:
             raise RuntimeError(st.message)
 
-    def config(self):
-        return {"workload": f"fused_elementwise_relu_affine_mul_sigmoid_{self.n}_f32", "n": self.n, "a": self.a,
-                "b": self.b, "input": "U(-4,4) seed 0",
-                "l2": f"rotating {self.nbuf} input/output pairs ({self.nbuf * 8 * self.n >> 20} MiB > 126 MB L2)",
-                "api": "fer_tensor_run_affine_f32 (fusion RELU|MUL_SIGMOID_INPUT)"}
+    @staticmethod
+    def describe(world, n=1 << 20):
+        nbuf = max(3, (384 << 20) // (8 * n))
+        return {"workload": f"fused_elementwise_relu_affine_mul_sigmoid_{n}_f32", "n": n, "a": 1.5,
+                "b": -0.25, "input": "U(-4,4) seed 0",
+                "l2": f"rotating {nbuf} input/output pairs ({nbuf * 8 * n >> 20} MiB > 126 MB L2)",
+                "api": "fer_tensor_run_affine_f32 (fusion RELU|MUL_SIGMOID_INPUT)", "parallelism": f"replicas x{world}"}
 
-    def e2e_step(self, hx, hy):
-        bx, by = self.pairs[0]
-        self.s.upload(bx, hx)
-        self.step(0)
-        self.s.download(by, hy)
+    def roofline(self, kern_ms):
+        r = super().roofline(kern_ms)
+        r["kernel"] = "fer_chain_v4 (JIT)"
+        return r
 
-    def cpu(self, orc, threads, reps=20):
-        y = np.empty_like(self.x)
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            orc.orc_chain_f32(self.x.ctypes.data_as(C.c_void_p), y.ctypes.data_as(C.c_void_p), self.n,
-                              C.c_float(self.a), C.c_float(self.b), threads)
-        dt = (time.perf_counter() - t0) / reps
-        return self.bytes_per_step / dt / 1e9, f"full 2^20 batch x{reps}"
+    @staticmethod
+    def cpu(threads, reps=20):
+        from fercuda_b200 import synth
+        from tests import oracle_lib
 
-
-WORKLOADS = {"softmax_layernorm": RowsWorkload, "fused_elementwise": ChainWorkload}
-
-
-# ------------------------------------------------------------------ main
-
-def host_threads():
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
-
-
-def run_reference(args, rank, world):
-    """The reference's CPU implementation of the path (oracle port), rank 0."""
-    if rank != 0:
-        return
-    from fercuda_b200 import synth
-    from tests import oracle_lib
-
-    orc = oracle_lib.load()
-    threads = host_threads()
-    if args.workload == "softmax_layernorm":
-        x = synth.softmax_layernorm_input()
-        rows, cols = x.shape
-        y = np.empty_like(x)
-        fn = lambda: orc.orc_softmax_layernorm_rows_f32(x.ctypes.data_as(C.c_void_p), y.ctypes.data_as(C.c_void_p),
-                                                        rows, cols, C.c_float(1e-5), threads)
-        nbytes = 8 * rows * cols
-        cfg = RowsWorkload.config(type("W", (), {"rows": rows, "cols": cols, "eps": 1e-5})())
-    else:
         x = synth.fused_elementwise_input()
         y = np.empty_like(x)
+        orc = oracle_lib.load()
         fn = lambda: orc.orc_chain_f32(x.ctypes.data_as(C.c_void_p), y.ctypes.data_as(C.c_void_p), x.size,
                                        C.c_float(1.5), C.c_float(-0.25), threads)
-        nbytes = 8 * x.size
-        cfg = {"workload": f"fused_elementwise_relu_affine_mul_sigmoid_{x.size}_f32"}
-    for _ in range(args.warmup):
         fn()
-    t0 = time.perf_counter()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        dt = (time.perf_counter() - t0) / reps
+        return 8 * x.size / dt / 1e9, f"full 2^20 batch, mean of {reps} passes", threads
+
+
+class Gemm:
+    """bf16 8192^3 -> f32, deterministic tcgen05 GEMM (fer_submit_gemm)."""
+    metric, unit, kernel = "deterministic GEMM TFLOP/s (bf16 in, f32 accumulate)", "TFLOP/s", "gemm_tc_8192"
+
+    def __init__(self, s, capi, synth, m=8192, n=8192, k=8192):
+        self.s, self.capi, self.m, self.n, self.k = s, capi, m, n, k
+        self.a, self.b = synth.gemm_inputs(m, n, k)
+        self.ba, self.bb = s.alloc(capi.FER_DTYPE_BF16, [m, k]), s.alloc(capi.FER_DTYPE_BF16, [k, n])
+        self.bo = s.alloc(capi.FER_DTYPE_F32, [m, n])
+        s.upload(self.ba, self.a)
+        s.upload(self.bb, self.b)
+        self.req = capi.fer_gemm_request_t(self.ba, self.bb, self.bo, 0, capi.FER_MEMORY_AUTO)
+        self.job = C.c_uint64()
+        self.units_per_step = 2.0 * m * n * k
+        self.launches_per_step = 1
+        self.h2d = 2 * (m * k + k * n)
+        self.d2h = 4 * m * n
+
+    def step(self, i):
+        st = self.s.call("fer_submit_gemm", C.byref(self.req), C.byref(self.job))
+        if st.code:
+            raise RuntimeError(st.message)
+
+    def config(self, world):
+        return self.describe(world)
+
+    @staticmethod
+    def describe(world, m=8192, n=8192, k=8192):
+        return {"workload": f"gemm_bf16_{m}x{n}x{k}_f32out", "m": m, "n": n, "k": k,
+                "input": "N(0, 1/sqrt(K)) seed 3", "l2": "operands 256 MiB + output 256 MiB exceed L2",
+                "api": "fer_submit_gemm", "parallelism": f"replicas x{world}"}
+
+    def e2e_prepare(self, torch):
+        self.ha = torch.from_numpy(self.a.reshape(-1).view(np.int16)).pin_memory().numpy()
+        self.hb = torch.from_numpy(self.b.reshape(-1).view(np.int16)).pin_memory().numpy()
+        self.hc = torch.empty(self.m * self.n, dtype=torch.float32).pin_memory().numpy()
+
+    def e2e_step(self):
+        self.s.upload(self.ba, self.ha)
+        self.s.upload(self.bb, self.hb)
+        self.step(0)
+        self.s.download(self.bo, self.hc)
+
+    def roofline(self, kern_ms):
+        pk, src = peak("bf16_tflops")
+        ach = self.units_per_step / (kern_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s", "frac": round(ach / pk, 4),
+                "traffic": profiled_traffic(self.kernel), "algorithmic_flops_per_launch": self.units_per_step,
+                "peak_source": src + " (burst)", "kernel": "gemm_bf16_tc_kernel", "kernel_ms_median": round(kern_ms, 5)}
+
+    @staticmethod
+    def cpu(threads, tiles=4):
+        """The reference's chain (sequential fmaf over K per output) on sampled
+        64x64 output tiles; TFLOP/s extrapolates per-output time to the matrix."""
+        from fercuda_b200 import synth
+        from tests import oracle_lib
+
+        a, b = synth.gemm_inputs()
+        m, k = a.shape
+        n = b.shape[1]
+        orc = oracle_lib.load()
+        out = np.empty((64, 64), np.float32)
+        t0 = time.perf_counter()
+        for t in range(tiles):
+            r0, c0 = (t * 1237) % (m - 64), (t * 3001) % (n - 64)
+            orc.orc_matmul_bf16_tile(oracle_lib.ptr(a), oracle_lib.ptr(b), oracle_lib.ptr(out), m, k, n, r0, r0 + 64,
+                                     c0, c0 + 64)
+        dt = time.perf_counter() - t0
+        return 2.0 * tiles * 64 * 64 * k / dt / 1e12, f"{tiles} sampled 64x64 output tiles, K=8192", 1
+
+
+class Transformer:
+    """Decoder-only transformer forward, batch-sharded (fer_transformer_forward)."""
+    metric, unit, kernel = METRIC_TOK, "tokens/s", "gemm_tc_transformer"
+
+    def __init__(self, s, capi, synth, rank=0, world=1, dist=None, torch=None):
+        cfg = synth.TRANSFORMER
+        self.s, self.capi, self.cfg = s, capi, cfg
+        self.world, self.rank = world, rank
+        L, d, h, F, V, S, B = (cfg[k] for k in ("layers", "d_model", "heads", "ffn", "vocab", "seq", "batch"))
+        if B % world:
+            raise SystemExit(f"global batch {B} does not split over {world} GPUs")
+        self.B_local, self.S, self.V = B // world, S, V
+        self.global_tokens = B * S
+        T = self.B_local * S
+        self.model = capi.Transformer(s, L, d, h, F, V, T, cfg["eps"])
+        if rank == 0:
+            self.model.init_weights(cfg["weight_seed"], 0.02)
+        if world > 1:
+            self._broadcast_weights(dist, torch)
+        u = synth.uniform01(cfg["token_seed"], B * S)
+        toks = np.minimum((u * V).astype(np.int32), V - 1).reshape(B, S)
+        self.toks = np.ascontiguousarray(toks[rank * self.B_local:(rank + 1) * self.B_local])
+        self.bt = s.alloc(capi.FER_DTYPE_I32, [self.B_local, S])
+        self.bl = s.alloc(capi.FER_DTYPE_F32, [self.B_local, S, V])
+        s.upload(self.bt, self.toks)
+        self.units_per_step = self.global_tokens
+        self.launches_per_step = 3 + 7 * L
+        self.h2d = 4 * T
+        self.d2h = 4 * T * V
+
+    def _broadcast_weights(self, dist, torch):
+        """Rank 0's weights reach every rank once, over NCCL (NVLink/NVSwitch)."""
+        wb = self.model.weight_buffer()
+        ptr = self.s.ptr_of(wb)
+        nbytes = 2 * self.model.weight_elements()
+
+        class CAI:
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                        "strides": None}
+
+        torch.cuda.synchronize()
+        t = torch.as_tensor(CAI(), device="cuda")
+        dist.broadcast(t, src=0)
+        torch.cuda.synchronize()
+        self.broadcast_bytes = nbytes
+
+    def step(self, i):
+        self.model.forward(self.bt, self.bl)
+
+    def config(self, world):
+        return self.describe(world)
+
+    @staticmethod
+    def describe(world):
+        from fercuda_b200 import synth
+
+        c = synth.TRANSFORMER
+        return {"workload": "decoder_transformer_fwd_L8_d1024_h16_F4096_V32000_S512_B64", "model": "decoder-only pre-LN",
+                "layers": c["layers"], "d_model": c["d_model"], "heads": c["heads"], "ffn": c["ffn"],
+                "vocab": c["vocab"], "seq_len": c["seq"], "global_batch": c["batch"], "local_batch": c["batch"] // world,
+                "weights": "bf16 N(0,0.02) seed 4 (device-generated on rank 0, NCCL broadcast once)",
+                "tokens": "uniform seed 5", "parallelism": f"dp{world} (batch-sharded, no per-step collective)",
+                "l2": "weights 333 MB + activations > 1 GB per step exceed L2", "api": "fer_transformer_forward"}
+
+    def e2e_prepare(self, torch):
+        self.ht = torch.from_numpy(self.toks.reshape(-1)).pin_memory().numpy()
+        self.hl = torch.empty(self.B_local * self.S * self.V, dtype=torch.float32).pin_memory().numpy()
+
+    def e2e_step(self):
+        self.s.upload(self.bt, self.ht)
+        self.step(0)
+        self.s.download(self.bl, self.hl)
+
+    def roofline_from_profile(self, prof):
+        pk, src = peak("bf16_tflops")
+        ach = prof.gemm_flops / (prof.gemm_ms * 1e-3) / 1e12
+        per_launch = prof.gemm_flops / max(1, prof.forwards) / (4 * self.cfg["layers"] + 1)   # mean over the GEMMs
+        return {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
+                "frac": round(ach / pk, 4), "traffic": profiled_traffic(self.kernel),
+                "algorithmic_flops_per_launch": round(per_launch), "peak_source": src + " (burst)",
+                "kernel": "gemm_bf16_tc_kernel (all GEMMs of the forward)",
+                "share_of_forward": round(prof.gemm_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4),
+                "attention_tflops": round(prof.attn_flops / (prof.attn_ms * 1e-3) / 1e12, 1) if prof.attn_ms else None,
+                "attention_share": round(prof.attn_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4),
+                "norm_share": round(prof.norm_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4)}
+
+    @staticmethod
+    def cpu(threads, seqs=1):
+        """numpy restatement (oracle/transformer_ref.py) on `seqs` full
+        sequences of 512 tokens; weights from numpy's generator with the same
+        distribution (the oracle's timing does not depend on the values)."""
+        from fercuda_b200 import synth
+        from oracle import transformer_ref as ref
+
+        c = synth.TRANSFORMER
+        if not hasattr(Transformer, "_cpu_w"):
+            o = ref.weight_offsets(c["layers"], c["d_model"], c["ffn"], c["vocab"])
+            w = np.random.default_rng(c["weight_seed"]).standard_normal(o["total"], dtype=np.float32)
+            w *= np.float32(0.02)
+            Transformer._cpu_w = (w.view(np.uint32) >> 16).astype(np.uint16)
+        wbits = Transformer._cpu_w
+        toks = np.minimum((synth.uniform01(c["token_seed"], seqs * c["seq"]) * c["vocab"]).astype(np.int32),
+                          c["vocab"] - 1).reshape(seqs, c["seq"])
+        t0 = time.perf_counter()
+        ref.forward(toks, wbits, c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"], c["eps"])
+        dt = time.perf_counter() - t0
+        return seqs * c["seq"] / dt, f"{seqs} sequence(s) x 512 tokens through the numpy restatement", threads
+
+
+class Tlsf:
+    """1M-op alloc/free trace through the TLSF pool, each block filled by a kernel."""
+    metric, unit, kernel = "TLSF alloc latency p50 (ns)", "ns", None
+
+    def __init__(self, s, capi, synth):
+        self.s, self.capi, self.synth = s, capi, synth
+
+    def run(self, ops=None, cmp_ops=50_000):
+        import ctypes
+
+        lib = ctypes.CDLL(str(self.capi.LIBDIR / "libfercuda_bench.so"))
+        core = self.capi.core()
+        lib.fer_bench_pool_replay.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p,
+                                              C.c_void_p, C.POINTER(C.c_size_t), C.c_void_p, C.POINTER(C.c_size_t),
+                                              C.POINTER(C.c_uint64), C.POINTER(C.c_double)]
+        trace = self.synth.tlsf_trace(ops=ops)
+        cfg = core.gpu_hot_default_config()
+        cfg.fixed_pool_size = 80 << 30
+        cfg.min_pool_size = 0
+        rt = core.gpu_hot_init_with_config(int(os.environ.get("LOCAL_RANK", "0")), b"bench", C.byref(cfg))
+        if not rt:
+            raise RuntimeError("could not create an 80 GiB pool")
+        stream = core.gpu_hot_get_stream(rt, 0)
+        res = {}
+        for name, use_cm, tr in (("tlsf", 0, trace), ("cudaMalloc", 1, trace[:cmp_ops]),
+                                 ("tlsf_same_sample", 0, trace[:cmp_ops])):
+            tr = np.ascontiguousarray(tr)   # a prefix of the trace frees only its own allocations
+            na_max = int((tr > 0).sum())
+            an = np.zeros(max(1, na_max), np.uint32)
+            fn = np.zeros(max(1, len(tr) - na_max), np.uint32)
+            na, nf, fb, wall = C.c_size_t(), C.c_size_t(), C.c_uint64(), C.c_double()
+            rc = lib.fer_bench_pool_replay(rt if not use_cm else None, use_cm, tr.ctypes.data_as(C.c_void_p), len(tr),
+                                           1, stream, an.ctypes.data_as(C.c_void_p), C.byref(na),
+                                           fn.ctypes.data_as(C.c_void_p), C.byref(nf), C.byref(fb), C.byref(wall))
+            a, f = an[:na.value], fn[:nf.value]
+            res[name] = {"rc": rc, "ops": len(tr), "allocs": int(na.value), "frees": int(nf.value),
+                         "alloc_p50_ns": float(np.percentile(a, 50)) if a.size else None,
+                         "alloc_p99_ns": float(np.percentile(a, 99)) if a.size else None,
+                         "free_p50_ns": float(np.percentile(f, 50)) if f.size else None,
+                         "free_p99_ns": float(np.percentile(f, 99)) if f.size else None,
+                         "fill_bytes": int(fb.value), "wall_s": round(wall.value, 3)}
+        core.gpu_hot_shutdown(rt)
+        return res
+
+    @staticmethod
+    def host_replay(lib_alloc, lib_free, handle, trace):
+        """Per-op latency (ns) of a TLSF's bookkeeping over `trace`, timed in C
+        (fer_bench_fn_replay) with the allocator's own entry points."""
+        from fercuda_b200 import capi
+
+        bench = C.CDLL(str(capi.LIBDIR / "libfercuda_bench.so"))
+        bench.fer_bench_fn_replay.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
+                                              C.POINTER(C.c_size_t), C.c_void_p, C.POINTER(C.c_size_t),
+                                              C.POINTER(C.c_double)]
+        tr = np.ascontiguousarray(trace, np.int64)
+        na_max = int((tr > 0).sum())
+        an = np.zeros(max(1, na_max), np.uint32)
+        fn = np.zeros(max(1, len(tr) - na_max), np.uint32)
+        na, nf, wall = C.c_size_t(), C.c_size_t(), C.c_double()
+        addr = lambda f: C.cast(f, C.c_void_p).value
+        rc = bench.fer_bench_fn_replay(addr(lib_alloc), addr(lib_free), handle, tr.ctypes.data_as(C.c_void_p), len(tr),
+                                       an.ctypes.data_as(C.c_void_p), C.byref(na), fn.ctypes.data_as(C.c_void_p),
+                                       C.byref(nf), C.byref(wall))
+        a, f = an[:na.value], fn[:nf.value]
+        return {"rc": rc, "ops": len(tr), "alloc_p50_ns": float(np.percentile(a, 50)),
+                "alloc_p99_ns": float(np.percentile(a, 99)), "free_p50_ns": float(np.percentile(f, 50)),
+                "free_p99_ns": float(np.percentile(f, 99)), "wall_s": round(wall.value, 3)}
+
+    @staticmethod
+    def cpu_reference(ops=1_000_000):
+        """The reference TLSF (oracle/_ref, compiled from its own sources) and
+        this package's TLSF, both host-only over the same fake 80 GiB range,
+        replaying the same trace: allocator bookkeeping latency per op."""
+        from fercuda_b200 import capi, synth
+        from tests import oracle_lib
+
+        ref = oracle_lib.ref_tlsf()
+        if ref is None:
+            return None
+        trace = synth.tlsf_trace(ops=ops)
+        base = C.c_void_p(1 << 40)
+        out = {}
+        for name, lib in (("reference", ref), ("fercuda_b200", capi.core())):
+            lib.ptx_tlsf_create_from_pool.restype = C.c_void_p
+            lib.ptx_tlsf_create_from_pool.argtypes = [C.c_void_p, C.c_size_t, C.c_bool]
+            lib.ptx_tlsf_set_warnings_enabled.argtypes = [C.c_void_p, C.c_bool]
+            lib.ptx_tlsf_destroy.argtypes = [C.c_void_p]
+            h = lib.ptx_tlsf_create_from_pool(base, 80 << 30, False)
+            lib.ptx_tlsf_set_warnings_enabled(h, False)
+            out[name] = Tlsf.host_replay(lib.ptx_tlsf_alloc, lib.ptx_tlsf_free, h, trace)
+            lib.ptx_tlsf_destroy(h)
+        out["note"] = "host-only bookkeeping over a fake range, timed in C around each call, 1 thread"
+        return out
+
+
+WORKLOADS = {"transformer": Transformer, "softmax_layernorm": Rows, "fused_elementwise": Chain, "gemm": Gemm,
+             "tlsf": Tlsf}
+
+
+# ================================================================ runners
+
+
+def timed_steps(wl, torch, stream, steps, warmup, dist, world, per_launch=True):
+    for i in range(warmup):
+        wl.step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)] if per_launch else []
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)] if per_launch else []
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0.record(stream)
+    for i in range(steps):
+        if per_launch:
+            starts[i].record(stream)
+        wl.step(warmup + i)
+        if per_launch:
+            ends[i].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed = t0.elapsed_time(t1)
+    kern = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    return elapsed, kern
+
+
+def max_over_ranks(v, torch, dist, world):
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def subresults(s, capi, synth, torch, stream):
+    """Short measurements of the other workloads (one GPU)."""
+    out = {}
+    for name, cls, steps in (("softmax_layernorm", Rows, 50), ("fused_elementwise", Chain, 200), ("gemm", Gemm, 10)):
+        wl = cls(s, capi, synth)
+        el, kern = timed_steps(wl, torch, stream, steps, 5, None, 1)
+        med = float(np.median(kern))
+        unit_scale = 1e9 if cls is not Gemm else 1e12
+        out[name] = {"metric": cls.metric, "value": round(wl.units_per_step * steps / (el * 1e-3) / unit_scale, 2),
+                     "unit": cls.unit, "steps": steps, "config": wl.config(1), "roofline": wl.roofline(med),
+                     "device_error_bits": s.device_errors()}
+        if cls is Gemm:
+            y0, y1 = np.empty((wl.m, wl.n), np.float32), np.empty((wl.m, wl.n), np.float32)
+            s.download(wl.bo, y0)
+            wl.step(0)
+            s.download(wl.bo, y1)
+            out[name]["bit_identical_rerun"] = bool(np.array_equal(y0.view(np.uint32), y1.view(np.uint32)))
+            for b in (wl.ba, wl.bb, wl.bo):
+                s.free(b)
+        else:
+            for bx, by in wl.pairs:
+                s.free(bx)
+                s.free(by)
+    tl = Tlsf(s, capi, synth).run(ops=100_000)
+    out["tlsf"] = {"metric": Tlsf.metric, "value": tl["tlsf"]["alloc_p50_ns"], "unit": "ns", "results": tl,
+                   "sample": "first 100k ops of the 1M-op trace (full trace: --workload tlsf)",
+                   "reference_tlsf_host": Tlsf.cpu_reference(ops=100_000)}
+    return out
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    threads = host_threads()
+    cls = WORKLOADS[args.workload]
+    if cls is Tlsf:
+        r = Tlsf.cpu_reference()
+        v = r["reference"]["alloc_p50_ns"] if r else None
+        line = {"metric": Tlsf.metric, "value": v, "unit": "ns", "impl": "reference",
+                "n_gpus": args.gpus, "steps": 1, "warmup": 0, "higher_is_better": False, "results": r,
+                "cpu_baseline": {"value": v, "unit": "ns", "cores": 1,
+                                 "kind": "reference", "sample": "full 1M-op trace, reference TLSF built from source"},
+                "e2e": {"value": v, "unit": "ns", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        emit(line)
+        return
+    vals = []
+    for _ in range(args.warmup if cls is not Transformer else 1):
+        cls.cpu(threads)
     for _ in range(args.steps):
-        fn()
-    dt = time.perf_counter() - t0
-    v = nbytes * args.steps / dt / 1e9
-    line = {"metric": "HBM GB/s (fused elementwise, softmax)", "value": round(v, 3), "unit": "GB/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg, "impl": "reference",
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": "full batch per step (oracle/oracle.c restatement of the reference kernels)"},
-            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+        v, sample, cores = cls.cpu(threads)
+        vals.append(v)
+    v = float(np.mean(vals))
+    line = {"metric": cls.metric, "value": round(v, 4), "unit": cls.unit, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong" if cls is Transformer else "weak",
+            "vs_baseline": None, "dtype": "bf16" if cls in (Transformer, Gemm) else "f32", "data": "synthetic",
+            "config": cls.describe(args.gpus), "impl": "reference",
+            "cpu_baseline": {"value": round(v, 4), "unit": cls.unit, "cores": cores, "kind": "port",
+                             "sample": sample + " (oracle/, restatement of the reference's path)"},
+            "e2e": {"value": round(v, 4), "unit": cls.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    emit(line)
+
+
+def emit(line: dict) -> None:
+    """The result line goes to the process's original stdout; everything the
+    native libraries print goes to stderr (fd 1 is redirected in main)."""
+    os.write(_OUT_FD, (json.dumps(line) + "\n").encode())
+
+
+_OUT_FD = 1
 
 
 def main():
+    global _OUT_FD
+    _OUT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="softmax_layernorm", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="transformer", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-subresults", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        run_reference(args, rank)
         return
 
     import torch
@@ -290,99 +673,106 @@ def main():
 
     torch.cuda.set_device(local)
     if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
 
     from fercuda_b200 import capi, synth
 
-    s = capi.Session(local, pool_bytes=2 << 30)
-    wl = WORKLOADS[args.workload](s, capi, synth)
+    cls = WORKLOADS[args.workload]
+    pool = 12 << 30 if cls is Transformer else 4 << 30
+    s = capi.Session(local, pool_bytes=pool)
     stream = torch.cuda.ExternalStream(s.stream())
 
-    for i in range(args.warmup):
-        wl.step(i)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    if cls is Tlsf:
+        if rank == 0:
+            tl = Tlsf(s, capi, synth).run()
+            line = {"metric": Tlsf.metric, "value": tl["tlsf"]["alloc_p50_ns"], "unit": "ns", "n_gpus": world,
+                    "steps": 1, "warmup": 0, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+                    "dtype": "int64", "data": "synthetic",
+                    "config": {"workload": "tlsf_stress_1M_ops_seed2", "pool": "80 GiB", "fill": "fer_fill_u32 per alloc"},
+                    "results": tl, "host_only": (host := Tlsf.cpu_reference()),
+                    "cpu_baseline": {"value": ((host or {}).get("reference") or {}).get("alloc_p50_ns"),
+                                                    "unit": "ns", "cores": 1, "kind": "reference",
+                                                    "sample": "full trace, reference TLSF host-only"}}
+            emit(line)
+        s.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    wl = cls(s, capi, synth, rank=rank, world=world, dist=dist, torch=torch) if cls is Transformer \
+        else cls(s, capi, synth)
 
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    t_all0, t_all1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    time.sleep(0.25)
     clocks.mark(True)
-    t_all0.record(stream)
-    for i in range(args.steps):
-        starts[i].record(stream)
-        wl.step(args.warmup + i)
-        ends[i].record(stream)
-    t_all1.record(stream)
-    torch.cuda.synchronize()
+    elapsed, kern = timed_steps(wl, torch, stream, args.steps, args.warmup, dist, world,
+                                per_launch=cls is not Transformer)
     clocks.mark(False)
-    if world > 1:
-        dist.barrier()
     clk = clocks.stop()
-    elapsed_ms = t_all0.elapsed_time(t_all1)
-    kern_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms = float(t.item())
+    elapsed = max_over_ranks(elapsed, torch, dist, world)
     errs = s.device_errors()
+    prof = None
+    if cls is Transformer:
+        # per-class device time from event pairs around every launch, on a
+        # separate pass so that the timed steps above carry no extra events
+        wl.model.profile(True)
+        for i in range(3):
+            wl.step(i)
+        prof = wl.model.profile_read()
+        wl.model.profile(False)
 
     # end to end through the C ABI with pinned host buffers
-    e2e_steps = args.e2e_steps or max(3, min(args.steps, 20))
-    hx = torch.from_numpy(wl.x.reshape(-1)).pin_memory().numpy()
-    hy = torch.empty(hx.size, dtype=torch.float32).pin_memory().numpy()
-    wl.e2e_step(hx, hy)
+    e2e_steps = args.e2e_steps or (5 if cls is Transformer else max(3, min(args.steps, 20)))
+    wl.e2e_prepare(torch)
+    wl.e2e_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0 = time.perf_counter()
     for _ in range(e2e_steps):
-        wl.e2e_step(hx, hy)
-    e2e_s = time.perf_counter() - e0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_s = float(te.item())
+        wl.e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - e0, torch, dist, world)
 
     if rank == 0:
-        peak, peak_src = peaks()
-        med = float(np.median(kern_ms))
-        achieved = wl.bytes_per_step / (med * 1e-3) / 1e9
-        value = wl.bytes_per_step * args.steps * world / (elapsed_ms * 1e-3) / 1e9
+        if cls is Transformer:
+            value = wl.global_tokens * args.steps / (elapsed * 1e-3)
+            e2e_v = wl.global_tokens * e2e_steps / e2e_s
+            roof = wl.roofline_from_profile(prof)
+            launches = int(round(prof.launches / max(1, prof.forwards))) * args.steps
+            unit_scale = 1.0
+        else:
+            unit_scale = 1e12 if cls is Gemm else 1e9
+            value = wl.units_per_step * args.steps * world / (elapsed * 1e-3) / unit_scale
+            e2e_v = wl.units_per_step * e2e_steps * world / e2e_s / unit_scale
+            roof = wl.roofline(float(np.median(kern)))
+            launches = wl.launches_per_step * args.steps
         cpu_base = None
         if world == 1:
-            from tests import oracle_lib
-
-            cv, sample = wl.cpu(oracle_lib.load(), host_threads())
-            cpu_base = {"value": round(cv, 3), "unit": "GB/s", "cores": host_threads(), "kind": "port",
-                        "sample": sample + ", oracle/oracle.c (C restatement of the reference kernels), all host threads"}
-        traffic = profiled_traffic(wl.kernel)
-        line = {
-            "metric": "HBM GB/s (fused elementwise, softmax)", "value": round(value, 2), "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(elapsed_ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": wl.config(),
-            "e2e": {"value": round(wl.bytes_per_step * e2e_steps * world / e2e_s / 1e9, 3), "unit": "GB/s",
-                    "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h, "steps": e2e_steps,
-                    "api": "fer_upload_bytes + submit + fer_download_bytes, pinned host buffers"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "algorithmic_bytes_per_launch": wl.bytes_per_step, "peak_source": peak_src,
-                         "kernel_ms_median": round(med, 5)},
-            "cpu_baseline": cpu_base,
-            "clocks": clk,
-            "gpu_launches": args.steps,
-            "device_error_bits": errs,
-        }
-        print(json.dumps(line), flush=True)
+            cv, sample, cores = cls.cpu(host_threads())
+            cpu_base = {"value": round(cv, 4), "unit": cls.unit, "cores": cores, "kind": "port",
+                        "sample": sample + " (oracle/, restatement of the reference's path)"}
+        line = {"metric": cls.metric, "value": round(value, 3), "unit": cls.unit, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps, 5),
+                "higher_is_better": True, "scaling": "strong" if cls is Transformer else "weak",
+                "vs_baseline": None, "dtype": "bf16" if cls in (Transformer, Gemm) else "f32", "data": "synthetic",
+                "config": wl.config(world),
+                "e2e": {"value": round(e2e_v, 3), "unit": cls.unit, "h2d_bytes_per_step": wl.h2d * world,
+                        "d2h_bytes_per_step": wl.d2h * world, "steps": e2e_steps,
+                        "api": "fer_upload_bytes + submit + fer_download_bytes (pinned host buffers)"},
+                "roofline": roof, "cpu_baseline": cpu_base, "clocks": clk, "gpu_launches": launches,
+                "device_error_bits": errs}
+        if cls is Transformer:
+            line["weight_broadcast_bytes"] = getattr(wl, "broadcast_bytes", 0)
+            line["profile_ms_per_forward"] = {k: round(getattr(prof, k) / max(1, prof.forwards), 4)
+                                              for k in ("gemm_ms", "attn_ms", "norm_ms", "other_ms")}
+        if world == 1 and cls is Transformer and not args.no_subresults:
+            wl.model.close()
+            s.free(wl.bl)
+            line["subresults"] = subresults(s, capi, synth, torch, stream)
+        emit(line)
+    if world > 1:
+        dist.barrier()
     s.close()
     if world > 1:
         dist.destroy_process_group()

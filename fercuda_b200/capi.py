@@ -173,6 +173,17 @@ class fer_gemm_request_t(C.Structure):
                 ("memory_regime", C.c_uint32)]
 
 
+class fer_transformer_config_t(C.Structure):
+    _fields_ = [("layers", C.c_uint32), ("d_model", C.c_uint32), ("heads", C.c_uint32), ("ffn", C.c_uint32),
+                ("vocab", C.c_uint32), ("max_tokens", C.c_uint32), ("eps", C.c_float), ("reserved", C.c_uint32)]
+
+
+class fer_transformer_profile_t(C.Structure):
+    _fields_ = [("gemm_ms", C.c_double), ("attn_ms", C.c_double), ("norm_ms", C.c_double), ("other_ms", C.c_double),
+                ("gemm_flops", C.c_double), ("attn_flops", C.c_double), ("forwards", C.c_uint64),
+                ("launches", C.c_uint64)]
+
+
 class fer_pool_stats_t(C.Structure):
     _fields_ = [("pool_bytes", C.c_uint64), ("allocated_bytes", C.c_uint64), ("peak_allocated_bytes", C.c_uint64),
                 ("largest_free_block", C.c_uint64), ("total_allocations", C.c_uint64), ("total_frees", C.c_uint64),
@@ -262,6 +273,13 @@ CAPI_PROTOTYPES = {
     "fer_submit_rows": (S, [P, C.POINTER(fer_rows_request_t), pu64]),
     "fer_jit_run_chain_f32": (S, [P, C.POINTER(fer_chain_op_t), u32, pu64, u32, u64, pu64]),
     "fer_submit_gemm": (S, [P, C.POINTER(fer_gemm_request_t), pu64]),
+    "fer_transformer_create": (S, [P, C.POINTER(fer_transformer_config_t), pu64]),
+    "fer_transformer_init_weights": (S, [P, u64, u64, f32]),
+    "fer_transformer_weight_buffer": (S, [P, u64, pu64]),
+    "fer_transformer_forward": (S, [P, u64, u64, u64, pu64]),
+    "fer_transformer_destroy": (S, [P, u64]),
+    "fer_transformer_profile": (S, [P, u64, u32]),
+    "fer_transformer_profile_read": (S, [P, u64, C.POINTER(fer_transformer_profile_t)]),
     "fer_session_device_errors": (S, [P, pu32, u8]),
     "fer_pool_get_stats": (S, [P, C.POINTER(fer_pool_stats_t)]),
     "fer_pool_alloc_raw": (S, [P, u64, C.POINTER(P)]),
@@ -479,6 +497,14 @@ class Session:
         check("fer_submit_gemm", self.call("fer_submit_gemm", C.byref(r), C.byref(job)))
         return job.value
 
+    def import_ptr(self, dtype: int, shape, ptr: int) -> int:
+        """Registers external device memory (e.g. a torch tensor) as a buffer."""
+        bid = C.c_uint64()
+        d = desc(dtype, shape)
+        check("fer_import_external_buffer",
+              self.call("fer_import_external_buffer", C.byref(d), C.c_void_p(ptr), FER_MEMORY_AUTO, C.byref(bid)))
+        return bid.value
+
     def chain(self, ops, inputs, out: int) -> int:
         arr = (fer_chain_op_t * len(ops))(*[fer_chain_op_t(*o) for o in ops])
         ins = (C.c_uint64 * len(inputs))(*inputs)
@@ -486,6 +512,58 @@ class Session:
         check("fer_jit_run_chain_f32",
               self.call("fer_jit_run_chain_f32", arr, len(ops), ins, len(inputs), out, C.byref(job)))
         return job.value
+
+
+class Transformer:
+    """A model of fer_transformer_* owned by a Session."""
+
+    def __init__(self, session: "Session", layers, d_model, heads, ffn, vocab, max_tokens, eps=1e-5):
+        self.s = session
+        self.cfg = fer_transformer_config_t(layers, d_model, heads, ffn, vocab, max_tokens, eps, 0)
+        mid = C.c_uint64()
+        check("fer_transformer_create", session.call("fer_transformer_create", C.byref(self.cfg), C.byref(mid)))
+        self.id = mid.value
+
+    def init_weights(self, seed: int, stddev: float = 0.02) -> None:
+        check("fer_transformer_init_weights", self.s.call("fer_transformer_init_weights", self.id, seed, stddev))
+
+    def weight_elements(self) -> int:
+        """bf16 elements of the weight buffer: embedding [V, d], then per layer
+        Wqkv [d, 3d], Wo [d, d], W1 [d, F], W2 [F, d], then the LM head [d, V],
+        each tensor starting on a 128-element boundary."""
+        up = lambda n: (n + 127) & ~127
+        c = self.cfg
+        d, F, V = c.d_model, c.ffn, c.vocab
+        off = up(V * d)
+        for _ in range(c.layers):
+            off = up(off + 3 * d * d)
+            off = up(off + d * d)
+            off = up(off + d * F)
+            off = up(off + F * d)
+        return up(off + d * V)
+
+    def weight_buffer(self) -> int:
+        b = C.c_uint64()
+        check("fer_transformer_weight_buffer", self.s.call("fer_transformer_weight_buffer", self.id, C.byref(b)))
+        return b.value
+
+    def forward(self, tokens: int, logits: int) -> int:
+        job = C.c_uint64()
+        check("fer_transformer_forward", self.s.call("fer_transformer_forward", self.id, tokens, logits, C.byref(job)))
+        return job.value
+
+    def profile(self, enable: bool) -> None:
+        check("fer_transformer_profile", self.s.call("fer_transformer_profile", self.id, 1 if enable else 0))
+
+    def profile_read(self) -> fer_transformer_profile_t:
+        p = fer_transformer_profile_t()
+        check("fer_transformer_profile_read", self.s.call("fer_transformer_profile_read", self.id, C.byref(p)))
+        return p
+
+    def close(self) -> None:
+        if self.id:
+            check("fer_transformer_destroy", self.s.call("fer_transformer_destroy", self.id))
+            self.id = 0
 
 
 def config1_chain(a: float, b: float):

@@ -46,6 +46,7 @@ fer_status_t check_desc(const fer_buffer_desc_t& d, size_t* numel, size_t* bytes
 
 Session::~Session() {
     if (stream) cudaStreamSynchronize(stream);
+    models.clear();   // their workspace returns to the pool before it goes away
     for (auto& kv : jobs) {
         Job& j = kv.second;
         if (j.ev) { cudaEventSynchronize(j.ev); cudaEventDestroy(j.ev); j.ev = nullptr; }

@@ -70,6 +70,7 @@ struct CustomAlloc {
 };
 
 class JitManager;
+struct Transformer;
 
 struct Session {
     int device = 0;
@@ -86,6 +87,8 @@ struct Session {
     size_t live_bytes[2] = {0, 0};   // CUDA_MALLOC / MANAGED budget per tier
     uint32_t* dev_err = nullptr;     // device error word (cudaMalloc'd)
     std::unique_ptr<JitManager> jit;
+    std::unordered_map<uint64_t, std::shared_ptr<Transformer>> models;
+    uint64_t next_model = 1;
 
     ~Session();
 
@@ -126,4 +129,13 @@ cudaError_t fer_matmul_bf16_f32_ref_order(const void* a, const void* b, float* c
                                           cudaStream_t stream);
 cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K, uint32_t out_dtype,
                              uint32_t* err, cudaStream_t stream);
+cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c, const float* resid, int M, int N, int K, int epi,
+                                uint32_t* err, cudaStream_t stream);
+cudaError_t fer_fill_normal_bf16(void* out, size_t n, uint64_t seed, float stddev, cudaStream_t s);
+cudaError_t fer_fill_f32(float* out, size_t n, float v, cudaStream_t s);
+cudaError_t fer_embed_f32(const int* tok, const void* emb, float* x, int T, int d, int vocab, uint32_t* err,
+                          cudaStream_t s);
+cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* out, int T, int d, float eps,
+                        cudaStream_t s);
+cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s);
 }

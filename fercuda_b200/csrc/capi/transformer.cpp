@@ -1,0 +1,301 @@
+// fer_transformer_*: the decoder-only transformer forward on this library's
+// kernels (gemm_tc.cu, xfmr_kernels.cu), every buffer from the session pool.
+//
+// The reference has no transformer of its own: its demo
+// (rust/deps/ferrite-torch/examples/transformer_demo.rs:18-70, 72-224) runs a
+// pre-LN block through libtorch on TLSF memory. This driver computes the same
+// block structure with token embedding, final LN and LM head added; per layer
+//   a   = LN1(x)                      ln_bf16            f32 -> bf16
+//   qkv = a @ Wqkv                    tcgen05 GEMM       bf16 out
+//   o   = causal_attention(qkv)       attn_causal        bf16 out
+//   x   = x + o @ Wo                  tcgen05 GEMM       f32 residual epilogue, in place
+//   a   = LN2(x)
+//   h   = gelu(a @ W1)                tcgen05 GEMM       exact-GELU bf16 epilogue
+//   x   = x + h @ W2                  tcgen05 GEMM       f32 residual epilogue
+// then logits = LN_f(x) @ Wlm in f32. Sequences of a batch never interact,
+// so any split of the batch across GPUs gives the same logits bit for bit.
+#include "session.hpp"
+
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <vector>
+
+namespace fer::capi {
+
+struct Transformer {
+    fer_transformer_config_t cfg{};
+    Session* S = nullptr;
+    uint64_t weight_buf = 0;
+    uint16_t* W = nullptr;      // bf16 blob
+    size_t w_elems = 0;
+    float* ln = nullptr;        // gamma / beta blob
+    size_t ln_elems = 0;
+    size_t off_emb = 0, off_lm = 0;
+    std::vector<size_t> off_qkv, off_o, off_w1, off_w2;
+    // workspace for max_tokens
+    float* x = nullptr;
+    uint16_t* a = nullptr;
+    uint16_t* qkv = nullptr;
+    uint16_t* att = nullptr;
+    uint16_t* hid = nullptr;
+    // profiling
+    bool profiling = false;
+    struct Mark { cudaEvent_t a, b; int cls; double flops; };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> spare;
+    fer_transformer_profile_t prof{};
+
+    cudaEvent_t event() {
+        cudaEvent_t e = nullptr;
+        if (!spare.empty()) {
+            e = spare.back();
+            spare.pop_back();
+        } else {
+            cudaEventCreate(&e);
+        }
+        return e;
+    }
+    void release_marks() {
+        for (auto& m : marks) {
+            spare.push_back(m.a);
+            spare.push_back(m.b);
+        }
+        marks.clear();
+    }
+
+    ~Transformer() {
+        if (!S) return;
+        release_marks();
+        for (cudaEvent_t e : spare) cudaEventDestroy(e);
+        for (void* p : {static_cast<void*>(x), static_cast<void*>(a), static_cast<void*>(qkv),
+                        static_cast<void*>(att), static_cast<void*>(hid), static_cast<void*>(ln)})
+            if (p) gpu_hot_free(S->pool, p);
+        auto it = S->buffers.find(weight_buf);
+        if (it != S->buffers.end()) {
+            S->free_bytes(it->second.ptr, it->second.regime, it->second.tier, it->second.bytes);
+            S->buffers.erase(it);
+        }
+    }
+};
+
+}  // namespace fer::capi
+
+using fer::capi::Buffer;
+using fer::capi::Session;
+using fer::capi::Transformer;
+using fer::capi::internal;
+using fer::capi::invalid;
+using fer::capi::not_found;
+using fer::capi::ok;
+
+namespace {
+
+enum : int { kEpiF32 = 0, kEpiBF16 = 1, kEpiGeluBF16 = 2, kEpiResidF32 = 3 };
+
+size_t up128(size_t n) { return (n + 127) & ~static_cast<size_t>(127); }
+
+Transformer* find_model(Session& S, uint64_t id) {
+    auto it = S.models.find(id);
+    return it == S.models.end() ? nullptr : it->second.get();
+}
+
+void* pool_alloc(Session& S, size_t bytes) { return gpu_hot_alloc(S.pool, (bytes + 255) & ~static_cast<size_t>(255)); }
+
+}  // namespace
+
+extern "C" {
+
+fer_status_t fer_transformer_create(fer_session_t* session, const fer_transformer_config_t* cfg, uint64_t* out_model) {
+    if (!session) return invalid("session is null");
+    if (!cfg || !out_model) return invalid("config or out_model is null");
+    Session& S = session->impl;
+    const fer_transformer_config_t c = *cfg;
+    if (c.layers == 0 || c.heads == 0 || c.d_model != c.heads * 64u) return invalid("transformer requires head_dim 64");
+    if (c.d_model % 256 || c.d_model > 4096) return invalid("transformer d_model must be a multiple of 256, <= 4096");
+    if (c.ffn == 0 || c.ffn % 8 || c.vocab == 0 || c.vocab % 8) return invalid("transformer ffn and vocab must be multiples of 8");
+    if (c.max_tokens == 0) return invalid("transformer max_tokens must be > 0");
+    auto m = std::shared_ptr<Transformer>(new Transformer());
+    m->cfg = c;
+    if (m->cfg.eps <= 0.0f) m->cfg.eps = 1e-5f;
+    const size_t d = c.d_model, F = c.ffn, V = c.vocab;
+    size_t off = 0;
+    m->off_emb = off;
+    off = up128(off + V * d);
+    for (uint32_t l = 0; l < c.layers; ++l) {
+        m->off_qkv.push_back(off);
+        off = up128(off + d * 3 * d);
+        m->off_o.push_back(off);
+        off = up128(off + d * d);
+        m->off_w1.push_back(off);
+        off = up128(off + d * F);
+        m->off_w2.push_back(off);
+        off = up128(off + F * d);
+    }
+    m->off_lm = off;
+    off = up128(off + d * V);
+    m->w_elems = off;
+    if (m->w_elems > 0xFFFFFFFFull) return invalid("transformer weights exceed a rank-1 buffer");
+    fer_buffer_desc_t wd{};
+    wd.dtype = FER_DTYPE_BF16;
+    wd.rank = 1;
+    wd.dims[0] = static_cast<uint32_t>(m->w_elems);
+    wd.immutable = 0;
+    void* wp = nullptr;
+    fer_status_t st = S.alloc_bytes(m->w_elems * 2, FER_ALLOC_TIER_MUTABLE, 0, FER_MEMORY_CUSTOM_POOL, &wp);
+    if (st.code != FER_STATUS_OK) return st;
+    S.add_buffer(wd, wp, FER_MEMORY_CUSTOM_POOL, false, nullptr, nullptr, &m->weight_buf);
+    m->W = static_cast<uint16_t*>(wp);
+    m->S = &S;
+    m->ln_elems = static_cast<size_t>(4 * c.layers + 2) * d;
+    m->ln = static_cast<float*>(pool_alloc(S, m->ln_elems * 4));
+    const size_t T = c.max_tokens;
+    m->x = static_cast<float*>(pool_alloc(S, T * d * 4));
+    m->a = static_cast<uint16_t*>(pool_alloc(S, T * d * 2));
+    m->qkv = static_cast<uint16_t*>(pool_alloc(S, T * 3 * d * 2));
+    m->att = static_cast<uint16_t*>(pool_alloc(S, T * d * 2));
+    m->hid = static_cast<uint16_t*>(pool_alloc(S, T * F * 2));
+    if (!m->ln || !m->x || !m->a || !m->qkv || !m->att || !m->hid) return internal("transformer workspace allocation failed");
+    const uint64_t id = S.next_model++;
+    S.models.emplace(id, m);
+    *out_model = id;
+    return fer_transformer_init_weights(session, id, 4, 0.02f);
+}
+
+fer_status_t fer_transformer_init_weights(fer_session_t* session, uint64_t model, uint64_t seed, float stddev) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    cudaError_t e = fer_fill_normal_bf16(m->W, m->w_elems, seed, stddev, S.stream);
+    const size_t d = m->cfg.d_model;
+    for (uint32_t blk = 0; blk < 2 * m->cfg.layers + 1 && e == cudaSuccess; ++blk) {
+        e = fer_fill_f32(m->ln + 2 * blk * d, d, 1.0f, S.stream);               // gamma
+        if (e == cudaSuccess) e = fer_fill_f32(m->ln + (2 * blk + 1) * d, d, 0.0f, S.stream);   // beta
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return internal("kernel launch failed");
+    }
+    return ok();
+}
+
+fer_status_t fer_transformer_weight_buffer(fer_session_t* session, uint64_t model, uint64_t* out_buffer_id) {
+    if (!session || !out_buffer_id) return invalid("session or out_buffer_id is null");
+    Transformer* m = find_model(session->impl, model);
+    if (!m) return not_found("model id not found");
+    *out_buffer_id = m->weight_buf;
+    return ok();
+}
+
+fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uint64_t tokens, uint64_t logits,
+                                     uint64_t* out_job_id) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    const Buffer* tb = S.find(tokens);
+    const Buffer* lb = S.find(logits);
+    if (!tb || !lb) return not_found("buffer id not found");
+    if (tb->desc.dtype != FER_DTYPE_I32 || (tb->desc.rank != 1 && tb->desc.rank != 2))
+        return invalid("tokens must be i32 [batch, seq] or [seq]");
+    const int B = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[0]) : 1;
+    const int Sq = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[1]) : static_cast<int>(tb->desc.dims[0]);
+    const size_t T = static_cast<size_t>(B) * Sq;
+    const fer_transformer_config_t& c = m->cfg;
+    if (T > c.max_tokens) return invalid("batch * seq exceeds the model's max_tokens");
+    if (lb->desc.dtype != FER_DTYPE_F32 || lb->numel != T * c.vocab) return invalid("logits must be f32 [batch, seq, vocab]");
+    const int d = static_cast<int>(c.d_model), F = static_cast<int>(c.ffn), V = static_cast<int>(c.vocab);
+    const int Ti = static_cast<int>(T);
+    cudaStream_t st = S.stream;
+    uint32_t* err = S.dev_err;
+    const uint16_t* W = m->W;
+    // Each launch goes through `run`, which brackets it with an event pair
+    // when profiling is on (class 0 gemm, 1 attention, 2 norm, 3 other).
+    cudaError_t e = cudaSuccess;
+    auto run = [&](int cls, double flops, auto&& launch) {
+        if (e != cudaSuccess) return;
+        if (!m->profiling) {
+            e = launch();
+            return;
+        }
+        Transformer::Mark mk{m->event(), m->event(), cls, flops};
+        cudaEventRecord(mk.a, st);
+        e = launch();
+        cudaEventRecord(mk.b, st);
+        m->marks.push_back(mk);
+    };
+    const double Td = static_cast<double>(T);
+    const double gq = 2.0 * Td * 3 * d * d, go = 2.0 * Td * d * d, g1f = 2.0 * Td * d * F, glm = 2.0 * Td * d * V;
+    // causal attention: S(S+1)/2 (query, key) pairs per sequence and head, 2*64 flops each for QK^T and for PV
+    const double ga = 4.0 * 64.0 * (static_cast<double>(Sq) * (Sq + 1) / 2.0) * B * c.heads;
+    run(3, 0.0, [&] { return fer_embed_f32(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, Ti, d, V, err, st); });
+    for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
+        const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
+        const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
+        const float* g2 = m->ln + (4 * l + 2) * static_cast<size_t>(d);
+        const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
+        run(2, 0.0, [&] { return fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st); });
+        run(0, gq, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_qkv[l], m->qkv, nullptr, Ti, 3 * d, d, kEpiBF16, err, st); });
+        run(1, ga, [&] { return fer_attn_causal(m->qkv, m->att, B, Sq, d, static_cast<int>(c.heads), st); });
+        run(0, go, [&] { return fer_gemm_bf16_tc_ex(m->att, W + m->off_o[l], m->x, m->x, Ti, d, d, kEpiResidF32, err, st); });
+        run(2, 0.0, [&] { return fer_ln_bf16(m->x, g2, b2, m->a, Ti, d, c.eps, st); });
+        run(0, g1f, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_w1[l], m->hid, nullptr, Ti, F, d, kEpiGeluBF16, err, st); });
+        run(0, g1f, [&] { return fer_gemm_bf16_tc_ex(m->hid, W + m->off_w2[l], m->x, m->x, Ti, d, F, kEpiResidF32, err, st); });
+    }
+    const float* gf = m->ln + (4 * static_cast<size_t>(c.layers)) * d;
+    const float* bf = gf + d;
+    run(2, 0.0, [&] { return fer_ln_bf16(m->x, gf, bf, m->a, Ti, d, c.eps, st); });
+    run(0, glm, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_lm, lb->ptr, nullptr, Ti, V, d, kEpiF32, err, st); });
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return internal("kernel launch failed");
+    }
+    if (m->profiling) m->prof.forwards++;
+    return S.make_job({}, out_job_id);
+}
+
+fer_status_t fer_transformer_profile(fer_session_t* session, uint64_t model, uint32_t enable) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    cudaStreamSynchronize(S.stream);
+    m->release_marks();
+    m->prof = fer_transformer_profile_t{};
+    m->profiling = enable != 0;
+    return ok();
+}
+
+fer_status_t fer_transformer_profile_read(fer_session_t* session, uint64_t model, fer_transformer_profile_t* out) {
+    if (!session || !out) return invalid("session or out is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    if (cudaStreamSynchronize(S.stream) != cudaSuccess) return internal("stream synchronize failed");
+    for (const auto& mk : m->marks) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, mk.a, mk.b) != cudaSuccess) return internal("event timing failed");
+        double* slot = mk.cls == 0 ? &m->prof.gemm_ms : mk.cls == 1 ? &m->prof.attn_ms : mk.cls == 2 ? &m->prof.norm_ms
+                                                                                         : &m->prof.other_ms;
+        *slot += ms;
+        if (mk.cls == 0) m->prof.gemm_flops += mk.flops;
+        if (mk.cls == 1) m->prof.attn_flops += mk.flops;
+        m->prof.launches++;
+    }
+    m->release_marks();
+    *out = m->prof;
+    return ok();
+}
+
+fer_status_t fer_transformer_destroy(fer_session_t* session, uint64_t model) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    auto it = S.models.find(model);
+    if (it == S.models.end()) return not_found("model id not found");
+    cudaStreamSynchronize(S.stream);
+    S.models.erase(it);
+    return ok();
+}
+
+}  // extern "C"

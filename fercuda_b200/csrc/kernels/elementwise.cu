@@ -152,3 +152,30 @@ void ptx_tensor_affine_f32(float* in, float* out, size_t n, float mul, float add
 }
 
 }  // extern "C"
+
+namespace {
+
+__global__ void fill_u32_kernel(uint4* __restrict__ dst, size_t n16, uint32_t v) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const uint4 w = make_uint4(v, v, v, v);
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += stride) dst[i] = w;
+}
+
+__global__ void fill_u8_tail(uint8_t* dst, size_t n, uint8_t v) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = v;
+}
+
+}  // namespace
+
+// Fills `bytes` bytes at dst (16-byte aligned) with the 32-bit pattern
+// `value` (the trailing bytes that do not fill a 16-byte word take its low byte).
+extern "C" cudaError_t fer_fill_u32(void* dst, size_t bytes, uint32_t value, cudaStream_t stream) {
+    if (bytes == 0) return cudaSuccess;
+    if (reinterpret_cast<uintptr_t>(dst) & 15u) return cudaErrorInvalidValue;
+    const size_t n16 = bytes / 16;
+    if (n16) fill_u32_kernel<<<grid_for(n16), kThreads, 0, stream>>>(static_cast<uint4*>(dst), n16, value);
+    const size_t tail = bytes - n16 * 16;
+    if (tail) fill_u8_tail<<<1, 16, 0, stream>>>(static_cast<uint8_t*>(dst) + n16 * 16, tail, static_cast<uint8_t>(value));
+    return cudaGetLastError();
+}

@@ -121,9 +121,72 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int* mb
     *nb = r / gm;
 }
 
+// Epilogue modes.
+enum : int { kEpiF32 = 0, kEpiBF16 = 1, kEpiGeluBF16 = 2, kEpiResidF32 = 3 };
+
+// Exact GELU, x * Phi(x) (erf form; the block's FFN activation).
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+// Stores 32 consecutive accumulator columns of one output row.
+__device__ __forceinline__ void store_row_chunk(const uint32_t (&r)[32], void* C, const float* resid, int row, int col0,
+                                                int N, int epi) {
+    const size_t base = static_cast<size_t>(row) * N + col0;
+    const bool full = col0 + 32 <= N;
+    if (epi == kEpiF32 || epi == kEpiResidF32) {
+        float* out = static_cast<float*>(C) + base;
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                       __uint_as_float(r[j + 3]));
+                if (epi == kEpiResidF32) {
+                    const float4 q = *reinterpret_cast<const float4*>(resid + base + j);
+                    v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
+                }
+                *reinterpret_cast<float4*>(out + j) = v;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) out[j] = __uint_as_float(r[j]) + (epi == kEpiResidF32 ? resid[base + j] : 0.0f);
+        }
+    } else {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(C) + base;
+        const bool gelu = epi == kEpiGeluBF16;
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                float f[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    f[u] = __uint_as_float(r[j + u]);
+                    if (gelu) f[u] = gelu_erf(f[u]);
+                }
+                uint4 v;
+                __nv_bfloat162 p0 = __floats2bfloat162_rn(f[0], f[1]);
+                __nv_bfloat162 p1 = __floats2bfloat162_rn(f[2], f[3]);
+                __nv_bfloat162 p2 = __floats2bfloat162_rn(f[4], f[5]);
+                __nv_bfloat162 p3 = __floats2bfloat162_rn(f[6], f[7]);
+                std::memcpy(&v.x, &p0, 4);
+                std::memcpy(&v.y, &p1, 4);
+                std::memcpy(&v.z, &p2, 4);
+                std::memcpy(&v.w, &p3, 4);
+                *reinterpret_cast<uint4*>(out + j) = v;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) {
+                    float f = __uint_as_float(r[j]);
+                    out[j] = __float2bfloat16_rn(gelu ? gelu_erf(f) : f);
+                }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C, int M,
-                        int N, int K, int out_bf16, uint32_t* err) {
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C,
+                        const float* resid, int M, int N, int K, int epi, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -252,43 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t r[32];
                 tmem_ld32(tbase + c * 32, r);
                 const int col0 = nb * BN + c * 32;
-                if (row < M && col0 < N) {
-                    if (!out_bf16) {
-                        float* out = static_cast<float*>(C) + static_cast<size_t>(row) * N + col0;
-                        if (col0 + 32 <= N) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(out + j) =
-                                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col0 + j < N) out[j] = __uint_as_float(r[j]);
-                        }
-                    } else {
-                        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(C) + static_cast<size_t>(row) * N + col0;
-                        if (col0 + 32 <= N) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 8) {
-                                uint4 v;
-                                __nv_bfloat162 p0 = __floats2bfloat162_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
-                                __nv_bfloat162 p1 = __floats2bfloat162_rn(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-                                __nv_bfloat162 p2 = __floats2bfloat162_rn(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5]));
-                                __nv_bfloat162 p3 = __floats2bfloat162_rn(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7]));
-                                std::memcpy(&v.x, &p0, 4);
-                                std::memcpy(&v.y, &p1, 4);
-                                std::memcpy(&v.z, &p2, 4);
-                                std::memcpy(&v.w, &p3, 4);
-                                *reinterpret_cast<uint4*>(out + j) = v;
-                            }
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col0 + j < N) out[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
-                        }
-                    }
-                }
+                if (row < M && col0 < N) store_row_chunk(r, C, resid, row, col0, N, epi);
             }
             tc_fence_before();
             __syncwarp();
@@ -349,14 +376,17 @@ int sm_count() {
 
 }  // namespace
 
-// out_dtype: 0 = f32, 2 = bf16 (fer_buffer_dtype_t codes). Requires K % 8 == 0
-// and N % 8 == 0 (16-byte row pitches for the tensor maps) and 16-byte aligned
-// operands; returns cudaErrorInvalidValue otherwise.
-extern "C" cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K,
-                                        uint32_t out_dtype, uint32_t* err, cudaStream_t stream) {
+// epi: 0 f32 out, 1 bf16 out, 2 bf16(gelu(acc)), 3 f32 out = acc + resid
+// (resid may be the output itself). Requires K % 8 == 0 and N % 8 == 0
+// (16-byte row pitches for the tensor maps) and 16-byte aligned operands;
+// returns cudaErrorInvalidValue otherwise.
+extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c, const float* resid, int M, int N,
+                                           int K, int epi, uint32_t* err, cudaStream_t stream) {
     if (M <= 0 || N <= 0 || K <= 0 || (K % 8) || (N % 8)) return cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u) return cudaErrorInvalidValue;
-    if (out_dtype != 0 && out_dtype != 2) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 15u)
+        return cudaErrorInvalidValue;
+    if (epi < kEpiF32 || epi > kEpiResidF32 || (epi == kEpiResidF32 && (!resid || (reinterpret_cast<uintptr_t>(resid) & 15u))))
+        return cudaErrorInvalidValue;
     CUtensorMap ma, mb;
     if (!make_map(&ma, a, static_cast<uint64_t>(M), static_cast<uint64_t>(K), BM) ||
         !make_map(&mb, b, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK))
@@ -369,6 +399,13 @@ extern "C" cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, i
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, c, M, N, K, out_dtype == 2 ? 1 : 0, err);
+    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, c, resid, M, N, K, epi, err);
     return cudaGetLastError();
+}
+
+// out_dtype: 0 = f32, 2 = bf16 (fer_buffer_dtype_t codes).
+extern "C" cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K,
+                                        uint32_t out_dtype, uint32_t* err, cudaStream_t stream) {
+    if (out_dtype != 0 && out_dtype != 2) return cudaErrorInvalidValue;
+    return fer_gemm_bf16_tc_ex(a, b, c, nullptr, M, N, K, out_dtype == 2 ? kEpiBF16 : kEpiF32, err, stream);
 }

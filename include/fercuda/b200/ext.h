@@ -99,6 +99,58 @@ typedef struct fer_gemm_request {
 
 fer_status_t fer_submit_gemm(fer_session_t* session, const fer_gemm_request_t* req, uint64_t* out_job_id);
 
+/* ---- decoder-only transformer forward --------------------------------------
+ * Pre-LN blocks (LN -> QKV -> causal multi-head attention -> out-proj +
+ * residual -> LN -> W1 -> exact GELU -> W2 + residual), final LN, LM head;
+ * token embedding, no biases, no positional embedding. Weights bf16, f32
+ * residual stream and accumulation, logits f32. head_dim must be 64,
+ * d_model a multiple of 256, ffn and vocab multiples of 8.
+ * All weights live in one session buffer (bf16, rank 1) so a caller can
+ * download it or broadcast it to other GPUs; layout, in elements, each
+ * tensor starting at a multiple of 128: embedding [vocab, d], then per layer
+ * Wqkv [d, 3d], Wo [d, d], W1 [d, ffn], W2 [ffn, d], then LM head [d, vocab]
+ * (x @ W convention, row-major). Layer-norm gamma / beta are f32, 1 and 0. */
+typedef struct fer_transformer_config {
+    uint32_t layers;
+    uint32_t d_model;
+    uint32_t heads;
+    uint32_t ffn;
+    uint32_t vocab;
+    uint32_t max_tokens;     /* largest batch*seq a forward may take (workspace size) */
+    float eps;
+    uint32_t reserved;
+} fer_transformer_config_t;
+
+fer_status_t fer_transformer_create(fer_session_t* session, const fer_transformer_config_t* cfg, uint64_t* out_model);
+/* Fills every weight with N(0, stddev) bf16 from `seed` (device-side
+ * splitmix64 + Box-Muller; element i of the weight buffer uses draws 2i+1 and
+ * 2i+2 of the seed's stream) and resets gamma to 1, beta to 0. */
+fer_status_t fer_transformer_init_weights(fer_session_t* session, uint64_t model, uint64_t seed, float stddev);
+/* Buffer id of the model's weight buffer (bf16, rank 1). */
+fer_status_t fer_transformer_weight_buffer(fer_session_t* session, uint64_t model, uint64_t* out_buffer_id);
+/* tokens: i32 [batch, seq] (or [seq]); logits: f32 [batch, seq, vocab] (or
+ * [batch*seq, vocab]). Sequences are independent (causal within each). */
+fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uint64_t tokens, uint64_t logits,
+                                     uint64_t* out_job_id);
+fer_status_t fer_transformer_destroy(fer_session_t* session, uint64_t model);
+
+/* Per-kernel-class timing of forwards: while enabled, every forward records a
+ * CUDA event pair around each of its launches on the session stream; reading
+ * synchronises the stream and sums the elapsed times. Enabling resets. */
+typedef struct fer_transformer_profile {
+    double gemm_ms;          /* tensor-core GEMMs (QKV, out-proj, W1, W2, LM head) */
+    double attn_ms;          /* causal attention */
+    double norm_ms;          /* layer norms */
+    double other_ms;         /* embedding */
+    double gemm_flops;       /* 2*M*N*K summed over the GEMM launches timed */
+    double attn_flops;       /* causal attention flops (QK^T and PV over unmasked pairs) */
+    uint64_t forwards;
+    uint64_t launches;
+} fer_transformer_profile_t;
+
+fer_status_t fer_transformer_profile(fer_session_t* session, uint64_t model, uint32_t enable);
+fer_status_t fer_transformer_profile_read(fer_session_t* session, uint64_t model, fer_transformer_profile_t* out);
+
 /* ---- diagnostics ------------------------------------------------------------ */
 
 /* Error bits that kernels of this session reported (bounded waits that ran

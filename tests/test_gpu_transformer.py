@@ -1,0 +1,129 @@
+"""Decoder-only transformer forward (fer_transformer_forward) against the
+numpy oracle (oracle/transformer_ref.py, which rounds to bf16 at the same
+points as the GPU path), plus the properties batch sharding relies on:
+sequences are independent, so any split of the batch gives bit-identical
+logits, and runs are bit-identical.
+
+Tolerance: the required bound for transformer logits is max relative error
+<= 2e-2 (normalised by max |reference|); the tests also hold 5e-3 on the
+2-layer model and 1e-2 on the 8-layer benchmark model, where rounding
+differences (online vs two-pass softmax, f32 vs f64 layer-norm statistics)
+compound over the layers."""
+import importlib.util
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from fercuda_b200 import capi, synth
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+_spec = importlib.util.spec_from_file_location("transformer_ref", ROOT / "oracle" / "transformer_ref.py")
+ref = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(ref)
+
+REQUIRED_TOL = 2e-2
+TIGHT = 5e-3
+TIGHT_DEEP = 1e-2
+
+
+def tokens_for(B, S, vocab, seed=5):
+    u = synth.uniform01(seed, B * S)
+    return np.minimum((u * vocab).astype(np.int32), vocab - 1).reshape(B, S)
+
+
+def run(session, model, toks, vocab):
+    import torch
+
+    B, S = toks.shape
+    t = torch.from_numpy(toks).cuda()
+    logits = torch.empty((B, S, vocab), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    bt = session.import_ptr(capi.FER_DTYPE_I32, [B, S], t.data_ptr())
+    bl = session.import_ptr(capi.FER_DTYPE_F32, [B, S, vocab], logits.data_ptr())
+    session.wait(model.forward(bt, bl))
+    session.free(bt)
+    session.free(bl)
+    assert session.device_errors() == 0
+    return logits
+
+
+def weights(session, model, n_elems):
+    w = np.empty(n_elems, np.uint16)
+    session.download(model.weight_buffer(), w)
+    return w
+
+
+def rel(y, r):
+    return float(np.abs(y.astype(np.float64) - r).max() / np.abs(r).max())
+
+
+SMALL = dict(layers=2, d_model=256, heads=4, ffn=512, vocab=1000)
+
+
+def test_small_model_vs_oracle_and_batch_split(session):
+    c = SMALL
+    B, S = 3, 192
+    m = capi.Transformer(session, c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"], B * S)
+    m.init_weights(4, 0.02)
+    toks = tokens_for(B, S, c["vocab"])
+    y = run(session, m, toks, c["vocab"]).cpu().numpy()
+    w = weights(session, m, ref.weight_offsets(c["layers"], c["d_model"], c["ffn"], c["vocab"])["total"])
+    r = ref.forward(toks, w, c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"])
+    err = rel(y, r)
+    assert err <= REQUIRED_TOL
+    assert err <= TIGHT, err
+    # each sequence alone gives the same bits as inside the batch
+    for b in range(B):
+        yb = run(session, m, toks[b:b + 1], c["vocab"]).cpu().numpy()
+        assert np.array_equal(yb[0].view(np.uint32), y[b].view(np.uint32))
+    # run to run
+    y2 = run(session, m, toks, c["vocab"]).cpu().numpy()
+    assert np.array_equal(y2.view(np.uint32), y.view(np.uint32))
+    m.close()
+
+
+def test_odd_sequence_length(session):
+    c = SMALL
+    B, S = 2, 77       # partial query and key blocks
+    m = capi.Transformer(session, c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"], B * S)
+    toks = tokens_for(B, S, c["vocab"], seed=9)
+    y = run(session, m, toks, c["vocab"]).cpu().numpy()
+    w = weights(session, m, ref.weight_offsets(c["layers"], c["d_model"], c["ffn"], c["vocab"])["total"])
+    r = ref.forward(toks, w, c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"])
+    assert rel(y, r) <= TIGHT
+    m.close()
+
+
+def test_full_size_model_sequences_vs_oracle():
+    """The benchmark model (8 layers, d 1024, 16 heads, ffn 4096, vocab 32000)
+    on 8 sequences of 512 tokens: sequences 0 and 7 against the oracle."""
+    cfg = synth.TRANSFORMER
+    L, d, h, F, V, S = cfg["layers"], cfg["d_model"], cfg["heads"], cfg["ffn"], cfg["vocab"], cfg["seq"]
+    B = 8
+    with capi.Session(0, pool_bytes=4 << 30) as s:
+        m = capi.Transformer(s, L, d, h, F, V, B * S)
+        m.init_weights(cfg["weight_seed"], 0.02)
+        toks = tokens_for(B, S, V, cfg["token_seed"])
+        y = run(s, m, toks, V).cpu().numpy()
+        assert np.isfinite(y).all()
+        w = weights(s, m, ref.weight_offsets(L, d, F, V)["total"])
+        for b in (0, 7):
+            r = ref.forward(toks[b:b + 1], w, L, d, h, F, V)
+            err = rel(y[b:b + 1], r)
+            assert err <= REQUIRED_TOL
+            assert err <= TIGHT_DEEP, (b, err)
+        m.close()
+
+
+def test_config_errors(session):
+    with pytest.raises(capi.FerError) as e:
+        capi.Transformer(session, 2, 256, 8, 512, 1000, 64)     # head_dim 32
+    assert e.value.code == capi.FER_STATUS_INVALID_ARGUMENT
+    m = capi.Transformer(session, 1, 256, 4, 512, 1000, 64)
+    toks = tokens_for(1, 128, 1000)
+    with pytest.raises(capi.FerError):
+        run(session, m, toks, 1000)                              # 128 tokens > max_tokens 64
+    m.close()
