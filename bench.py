@@ -42,6 +42,8 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from fercuda_b200 import sharding  # noqa: E402  (numpy only; no native library)
+
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC_HBM = "HBM GB/s (fused elementwise, softmax)"
 METRIC_TOK = "transformer fwd tokens/s"
@@ -263,11 +265,17 @@ class Gemm:
 
     def __init__(self, s, capi, synth, m=8192, n=8192, k=8192):
         self.s, self.capi, self.m, self.n, self.k = s, capi, m, n, k
-        self.a, self.b = synth.gemm_inputs(m, n, k)
-        self.ba, self.bb = s.alloc(capi.FER_DTYPE_BF16, [m, k]), s.alloc(capi.FER_DTYPE_BF16, [k, n])
+        # A is the first m*k draws of the device generator's seed-3 stream, B the
+        # next k*n (one fill over both, then two buffer views of it)
+        self.bab = s.alloc(capi.FER_DTYPE_BF16, [m * k + k * n])
+        base = s.ptr_of(self.bab)
+        rc = capi.kernels().fer_fill_normal_bf16(C.c_void_p(base), m * k + k * n, synth.GEMM["seed"],
+                                                 C.c_float(1.0 / np.sqrt(k)), C.c_void_p(s.stream()))
+        if rc:
+            raise RuntimeError(f"fer_fill_normal_bf16 failed: {rc}")
+        self.ba = s.import_ptr(capi.FER_DTYPE_BF16, [m, k], base)
+        self.bb = s.import_ptr(capi.FER_DTYPE_BF16, [k, n], base + 2 * m * k)
         self.bo = s.alloc(capi.FER_DTYPE_F32, [m, n])
-        s.upload(self.ba, self.a)
-        s.upload(self.bb, self.b)
         self.req = capi.fer_gemm_request_t(self.ba, self.bb, self.bo, 0, capi.FER_MEMORY_AUTO)
         self.job = C.c_uint64()
         self.units_per_step = 2.0 * m * n * k
@@ -286,12 +294,15 @@ class Gemm:
     @staticmethod
     def describe(world, m=8192, n=8192, k=8192):
         return {"workload": f"gemm_bf16_{m}x{n}x{k}_f32out", "m": m, "n": n, "k": k,
-                "input": "N(0, 1/sqrt(K)) seed 3", "l2": "operands 256 MiB + output 256 MiB exceed L2",
+                "input": "N(0, 1/sqrt(K)) seed 3 (device generator: A the first M*K draws, B the next K*N)",
+                "l2": "operands 256 MiB + output 256 MiB exceed L2",
                 "api": "fer_submit_gemm", "parallelism": f"replicas x{world}"}
 
     def e2e_prepare(self, torch):
-        self.ha = torch.from_numpy(self.a.reshape(-1).view(np.int16)).pin_memory().numpy()
-        self.hb = torch.from_numpy(self.b.reshape(-1).view(np.int16)).pin_memory().numpy()
+        self.ha = torch.empty(self.m * self.k, dtype=torch.int16).pin_memory().numpy()
+        self.hb = torch.empty(self.k * self.n, dtype=torch.int16).pin_memory().numpy()
+        self.s.download(self.ba, self.ha)
+        self.s.download(self.bb, self.hb)
         self.hc = torch.empty(self.m * self.n, dtype=torch.float32).pin_memory().numpy()
 
     def e2e_step(self):
@@ -311,17 +322,19 @@ class Gemm:
     def cpu(threads, tiles=4):
         """The reference's chain (sequential fmaf over K per output) on sampled
         64x64 output tiles; TFLOP/s extrapolates per-output time to the matrix."""
-        from fercuda_b200 import synth
         from tests import oracle_lib
 
-        a, b = synth.gemm_inputs()
-        m, k = a.shape
-        n = b.shape[1]
+        # operand values do not change the chain's timing: numpy's generator
+        # with the workload's distribution, bf16 by truncation
+        m, n, k = 64 * tiles, 8192, 8192
+        rng = np.random.default_rng(3)
+        bits = lambda shape: (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+        a, b = bits((m, k)), bits((k, n))
         orc = oracle_lib.load()
         out = np.empty((64, 64), np.float32)
         t0 = time.perf_counter()
         for t in range(tiles):
-            r0, c0 = (t * 1237) % (m - 64), (t * 3001) % (n - 64)
+            r0, c0 = 64 * t, (t * 3001) % (n - 64)
             orc.orc_matmul_bf16_tile(oracle_lib.ptr(a), oracle_lib.ptr(b), oracle_lib.ptr(out), m, k, n, r0, r0 + 64,
                                      c0, c0 + 64)
         dt = time.perf_counter() - t0
@@ -332,8 +345,10 @@ class Transformer:
     """Decoder-only transformer forward, batch-sharded (fer_transformer_forward)."""
     metric, unit, kernel = METRIC_TOK, "tokens/s", "gemm_tc_transformer"
 
-    def __init__(self, s, capi, synth, rank=0, world=1, dist=None, torch=None):
-        cfg = synth.TRANSFORMER
+    def __init__(self, s, capi, synth, rank=0, world=1, dist=None, torch=None, batch=None):
+        cfg = dict(synth.TRANSFORMER)
+        if batch:
+            cfg["batch"] = batch
         self.s, self.capi, self.cfg = s, capi, cfg
         self.world, self.rank = world, rank
         L, d, h, F, V, S, B = (cfg[k] for k in ("layers", "d_model", "heads", "ffn", "vocab", "seq", "batch"))
@@ -349,7 +364,7 @@ class Transformer:
             self._broadcast_weights(dist, torch)
         u = synth.uniform01(cfg["token_seed"], B * S)
         toks = np.minimum((u * V).astype(np.int32), V - 1).reshape(B, S)
-        self.toks = np.ascontiguousarray(toks[rank * self.B_local:(rank + 1) * self.B_local])
+        self.toks = sharding.shard_tokens(toks, world, rank)
         self.bt = s.alloc(capi.FER_DTYPE_I32, [self.B_local, S])
         self.bl = s.alloc(capi.FER_DTYPE_F32, [self.B_local, S, V])
         s.upload(self.bt, self.toks)
@@ -360,32 +375,26 @@ class Transformer:
 
     def _broadcast_weights(self, dist, torch):
         """Rank 0's weights reach every rank once, over NCCL (NVLink/NVSwitch)."""
-        wb = self.model.weight_buffer()
-        ptr = self.s.ptr_of(wb)
-        nbytes = 2 * self.model.weight_elements()
-
-        class CAI:
-            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
-                                        "strides": None}
-
+        ptr = self.s.ptr_of(self.model.weight_buffer())
+        t = sharding.device_bytes_as_tensor(torch, ptr, 2 * self.model.weight_elements())
         torch.cuda.synchronize()
-        t = torch.as_tensor(CAI(), device="cuda")
-        dist.broadcast(t, src=0)
+        self.broadcast_bytes = sharding.broadcast_from_rank0(dist, t)
         torch.cuda.synchronize()
-        self.broadcast_bytes = nbytes
 
     def step(self, i):
         self.model.forward(self.bt, self.bl)
 
     def config(self, world):
-        return self.describe(world)
+        return self.describe(world, self.cfg["batch"])
 
     @staticmethod
-    def describe(world):
+    def describe(world, batch=None):
         from fercuda_b200 import synth
 
-        c = synth.TRANSFORMER
-        return {"workload": "decoder_transformer_fwd_L8_d1024_h16_F4096_V32000_S512_B64", "model": "decoder-only pre-LN",
+        c = dict(synth.TRANSFORMER)
+        c["batch"] = batch or c["batch"]
+        return {"workload": f"decoder_transformer_fwd_L8_d1024_h16_F4096_V32000_S512_B{c['batch']}",
+                "model": "decoder-only pre-LN",
                 "layers": c["layers"], "d_model": c["d_model"], "heads": c["heads"], "ffn": c["ffn"],
                 "vocab": c["vocab"], "seq_len": c["seq"], "global_batch": c["batch"], "local_batch": c["batch"] // world,
                 "weights": "bf16 N(0,0.02) seed 4 (device-generated on rank 0, NCCL broadcast once)",
@@ -568,10 +577,7 @@ def timed_steps(wl, torch, stream, steps, warmup, dist, world, per_launch=True):
 
 
 def max_over_ranks(v, torch, dist, world):
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return sharding.max_over_ranks(torch, dist, v, "cuda")
 
 
 def subresults(s, capi, synth, torch, stream):
@@ -585,13 +591,16 @@ def subresults(s, capi, synth, torch, stream):
         out[name] = {"metric": cls.metric, "value": round(wl.units_per_step * steps / (el * 1e-3) / unit_scale, 2),
                      "unit": cls.unit, "steps": steps, "config": wl.config(1), "roofline": wl.roofline(med),
                      "device_error_bits": s.device_errors()}
+        cv, sample, cores = cls.cpu(host_threads())
+        out[name]["cpu_baseline"] = {"value": round(cv, 6), "unit": cls.unit, "cores": cores, "kind": "port",
+                                     "sample": sample + " (oracle/, restatement of the reference's path)"}
         if cls is Gemm:
             y0, y1 = np.empty((wl.m, wl.n), np.float32), np.empty((wl.m, wl.n), np.float32)
             s.download(wl.bo, y0)
             wl.step(0)
             s.download(wl.bo, y1)
             out[name]["bit_identical_rerun"] = bool(np.array_equal(y0.view(np.uint32), y1.view(np.uint32)))
-            for b in (wl.ba, wl.bb, wl.bo):
+            for b in (wl.ba, wl.bb, wl.bo, wl.bab):
                 s.free(b)
         else:
             for bx, by in wl.pairs:
@@ -658,6 +667,8 @@ def main():
     ap.add_argument("--workload", default="transformer", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-subresults", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="transformer only: a smaller global batch (profiling case); default 64")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -699,7 +710,8 @@ def main():
             dist.destroy_process_group()
         return
 
-    wl = cls(s, capi, synth, rank=rank, world=world, dist=dist, torch=torch) if cls is Transformer \
+    wl = cls(s, capi, synth, rank=rank, world=world, dist=dist, torch=torch, batch=args.global_batch) \
+        if cls is Transformer \
         else cls(s, capi, synth)
 
     clocks = ClockSampler(local)

@@ -345,6 +345,8 @@ KERNEL_PROTOTYPES = {
     "ptx_tensor_softmax_layer_norm_f32": (None, [P, P, P, P, sz, sz, f32, P]),
     "ptx_tensor_layer_norm_rows_f32": (None, [P, P, P, P, sz, sz, f32, P]),
     "ptx_tensor_reduce_f32_noalloc": (C.c_int, [P, P, sz, C.c_int, P]),
+    # include/fercuda/b200/ext.h (native launchers)
+    "fer_fill_normal_bf16": (C.c_int, [P, sz, u64, f32, P]),
 }
 
 _LIBS: dict[str, C.CDLL] = {}
