@@ -18,8 +18,13 @@
 //               accumulators) and issues tcgen05.mma (M=128, N=256, K=16)
 //               from one thread; tcgen05.commit releases ring slots and
 //               hands finished accumulators to the epilogue
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, convert, store;
-//               runs while the MMA warp fills the other accumulator
+//   warps 2..9  epilogue, two warps per 32-lane TMEM quarter (one per
+//               128-column half): tcgen05.ld, convert (bf16 / GELU), write a
+//               32-row x 128-byte box into a swizzled shared staging buffer,
+//               and one lane issues a TMA tensor store of the box (or, for
+//               the in-place residual x += A.B, a TMA reduce-add, which adds
+//               each element exactly once in L2). Runs while the MMA warp
+//               fills the other accumulator.
 // Tile order: groups of 16 M-blocks, N-blocks inside a group, so a wave of
 // 148 CTAs touches ~16 A row-panels and ~9 B column-panels (fits in L2).
 // Every wait is bounded (about one second); on timeout the kernel records an
@@ -43,8 +48,10 @@ constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;              // 16 KiB
 constexpr int B_BYTES = BK * BN * 2;              // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;    // 48 KiB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-constexpr int kThreads = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int STAGING_BYTES = 32 * 128;           // one 32-row x 128-byte output box per epilogue warp
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGING_BYTES + 1024;
+constexpr int kThreads = 64 + 32 * EPI_WARPS;
 constexpr int GROUP_M = 16;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -127,66 +134,48 @@ enum : int { kEpiF32 = 0, kEpiBF16 = 1, kEpiGeluBF16 = 2, kEpiResidF32 = 3 };
 // Exact GELU, x * Phi(x) (erf form; the block's FFN activation).
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
-// Stores 32 consecutive accumulator columns of one output row.
-__device__ __forceinline__ void store_row_chunk(const uint32_t (&r)[32], void* C, const float* resid, int row, int col0,
-                                                int N, int epi) {
-    const size_t base = static_cast<size_t>(row) * N + col0;
-    const bool full = col0 + 32 <= N;
-    if (epi == kEpiF32 || epi == kEpiResidF32) {
-        float* out = static_cast<float*>(C) + base;
-        if (full) {
+// bf16 pair {lo, hi} (round to nearest even), lo in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t u;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(u) : "f"(hi), "f"(lo));
+    return u;
+}
+
+// One 128-byte row of a staging box: 16-byte chunk j of row r lives at
+// r*128 + ((j ^ (r & 7)) * 16), the layout a SWIZZLE_128B tensor map expects
+// of a 1024-byte aligned box (and 8 distinct banks groups per 8 lanes).
+__device__ __forceinline__ void stage_row(uint32_t sbase, int r, const uint32_t (&w)[32]) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                       __uint_as_float(r[j + 3]));
-                if (epi == kEpiResidF32) {
-                    const float4 q = *reinterpret_cast<const float4*>(resid + base + j);
-                    v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
-                }
-                *reinterpret_cast<float4*>(out + j) = v;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < N) out[j] = __uint_as_float(r[j]) + (epi == kEpiResidF32 ? resid[base + j] : 0.0f);
-        }
-    } else {
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(C) + base;
-        const bool gelu = epi == kEpiGeluBF16;
-        if (full) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-                float f[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    f[u] = __uint_as_float(r[j + u]);
-                    if (gelu) f[u] = gelu_erf(f[u]);
-                }
-                uint4 v;
-                __nv_bfloat162 p0 = __floats2bfloat162_rn(f[0], f[1]);
-                __nv_bfloat162 p1 = __floats2bfloat162_rn(f[2], f[3]);
-                __nv_bfloat162 p2 = __floats2bfloat162_rn(f[4], f[5]);
-                __nv_bfloat162 p3 = __floats2bfloat162_rn(f[6], f[7]);
-                std::memcpy(&v.x, &p0, 4);
-                std::memcpy(&v.y, &p1, 4);
-                std::memcpy(&v.z, &p2, 4);
-                std::memcpy(&v.w, &p3, 4);
-                *reinterpret_cast<uint4*>(out + j) = v;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < N) {
-                    float f = __uint_as_float(r[j]);
-                    out[j] = __float2bfloat16_rn(gelu ? gelu_erf(f) : f);
-                }
-        }
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t a = sbase + static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[4 * j]), "r"(w[4 * j + 1]),
+                     "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                     : "memory");
     }
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t ssrc, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(ssrc), "r"(x), "r"(y)
+                 : "memory");
+}
+
+// out[box] += staged[box], element by element in L2 (one add per element).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t ssrc, int x, int y) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(ssrc), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C,
-                        const float* resid, int M, int N, int K, int epi, uint32_t* err) {
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -203,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars.acc_full[b], 1);
-            mbar_init(&bars.acc_empty[b], 4);   // one arrival per epilogue warp
+            mbar_init(&bars.acc_empty[b], EPI_WARPS);   // one arrival per epilogue warp
         }
         bars.abort_flag = 0;
         fence_mbar_init();
@@ -293,9 +282,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
         }
     } else {
-        // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
+        // ---------------- epilogue warps 2..9: TMEM lanes 32*(warp%4) .., columns half*128 ..
         const int q = warp & 3;
-        const int row_in_tile = q * 32 + lane;
+        const int half = (warp - 2) >> 2;
+        const uint32_t stage = smem_addr(smem + STAGES * STAGE_BYTES + (warp - 2) * STAGING_BYTES);
+        const bool f32_out = epi == kEpiF32 || epi == kEpiResidF32;
+        const int chunk_cols = f32_out ? 32 : 64;            // one 128-byte box row
+        const int n_chunks = (BN / 2) / chunk_cols;
         int local = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
             const int buf = local & 1;
@@ -308,19 +301,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             int mb, nb;
             tile_coords(t, num_m, num_n, &mb, &nb);
-            const int row = mb * BM + row_in_tile;
-            const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+            const int row0 = mb * BM + q * 32;
+            const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(buf * BN + half * (BN / 2));
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tbase + c * 32, r);
-                const int col0 = nb * BN + c * 32;
-                if (row < M && col0 < N) store_row_chunk(r, C, resid, row, col0, N, epi);
+            for (int c = 0; c < n_chunks; ++c) {
+                uint32_t w[32];
+                if (f32_out) {
+                    tmem_ld32(tbase + c * 32, w);
+                } else {
+                    const bool gelu = epi == kEpiGeluBF16;
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 64 + h2 * 32, r);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            float a0 = __uint_as_float(r[2 * j]), a1 = __uint_as_float(r[2 * j + 1]);
+                            if (gelu) {
+                                a0 = gelu_erf(a0);
+                                a1 = gelu_erf(a1);
+                            }
+                            w[16 * h2 + j] = pack_bf16x2(a0, a1);
+                        }
+                    }
+                }
+                if (c == n_chunks - 1) {
+                    // every TMEM read of this accumulator is done: hand it back
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
+                }
+                // the previous box has been read out of the staging buffer
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+                stage_row(stage, lane, w);
+                fence_proxy_async_smem();
+                __syncwarp();
+                const int col0 = nb * BN + half * (BN / 2) + c * chunk_cols;
+                if (lane == 0 && row0 < M && col0 < N) {
+                    if (epi == kEpiResidF32) tma_reduce_add_2d(&tmC, stage, col0, row0);
+                    else tma_store_2d(&tmC, stage, col0, row0);
+                    bulk_commit();
+                }
+                __syncwarp();
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
         }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -350,16 +378,19 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box [box_rows, 64].
-bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// 2-D tensor map over a row-major [rows, cols] matrix of 2- or 4-byte
+// elements, box [box_rows, 128 bytes], 128-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+              CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
+    const uint32_t esize = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4u : 2u;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint64_t strides[1] = {cols * esize};
+    const cuuint32_t box[2] = {128u / esize, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -376,10 +407,11 @@ int sm_count() {
 
 }  // namespace
 
-// epi: 0 f32 out, 1 bf16 out, 2 bf16(gelu(acc)), 3 f32 out = acc + resid
-// (resid may be the output itself). Requires K % 8 == 0 and N % 8 == 0
-// (16-byte row pitches for the tensor maps) and 16-byte aligned operands;
-// returns cudaErrorInvalidValue otherwise.
+// epi: 0 f32 out, 1 bf16 out, 2 bf16(gelu(acc)), 3 f32 out = resid + acc.
+// With resid == c the residual add happens in place (TMA reduce-add); any
+// other resid is first copied into c (it must not partly overlap c).
+// Requires K % 8 == 0 and N % 8 == 0 (16-byte row pitches for the tensor
+// maps) and 16-byte aligned operands; returns cudaErrorInvalidValue otherwise.
 extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c, const float* resid, int M, int N,
                                            int K, int epi, uint32_t* err, cudaStream_t stream) {
     if (M <= 0 || N <= 0 || K <= 0 || (K % 8) || (N % 8)) return cudaErrorInvalidValue;
@@ -387,10 +419,20 @@ extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c
         return cudaErrorInvalidValue;
     if (epi < kEpiF32 || epi > kEpiResidF32 || (epi == kEpiResidF32 && (!resid || (reinterpret_cast<uintptr_t>(resid) & 15u))))
         return cudaErrorInvalidValue;
-    CUtensorMap ma, mb;
+    const bool f32_out = epi == kEpiF32 || epi == kEpiResidF32;
+    CUtensorMap ma, mb, mc;
     if (!make_map(&ma, a, static_cast<uint64_t>(M), static_cast<uint64_t>(K), BM) ||
-        !make_map(&mb, b, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK))
+        !make_map(&mb, b, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK) ||
+        !make_map(&mc, c, static_cast<uint64_t>(M), static_cast<uint64_t>(N), 32,
+                  f32_out ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
         return cudaErrorInvalidValue;
+    if (epi == kEpiResidF32 && resid != c) {
+        const size_t bytes = static_cast<size_t>(M) * N * sizeof(float);
+        const uintptr_t r0 = reinterpret_cast<uintptr_t>(resid), c0 = reinterpret_cast<uintptr_t>(c);
+        if (r0 < c0 + bytes && c0 < r0 + bytes) return cudaErrorInvalidValue;
+        cudaError_t e = cudaMemcpyAsync(c, resid, bytes, cudaMemcpyDeviceToDevice, stream);
+        if (e != cudaSuccess) return e;
+    }
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
@@ -399,7 +441,7 @@ extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, c, resid, M, N, K, epi, err);
+    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, mc, M, N, K, epi, err);
     return cudaGetLastError();
 }
 

@@ -1,6 +1,6 @@
 """Deterministic tcgen05 GEMM (fer_submit_gemm) on the GPU through the C ABI.
 
-Tolerance: the north-star bound for bf16-in / f32-accumulate GEMM is a max
+Tolerance: the required bound for bf16-in / f32-accumulate GEMM is a max
 relative error <= 2e-2 (normalised by max |reference|); products of bf16
 values are exact in f32, so the only difference to the reference's
 sequential-FMA chain is summation order, and the tests also hold the much
@@ -15,7 +15,7 @@ from tests import oracle_lib
 
 pytestmark = pytest.mark.gpu
 
-NORTH_STAR_TOL = 2e-2
+REQUIRED_TOL = 2e-2
 REL = 1e-4
 
 
@@ -45,7 +45,7 @@ def test_gemm_vs_float64(session, m, n, k):
     bufs, y = run_gemm(session, a, b)
     ref = synth.bf16_bits_to_f32(a).astype(np.float64) @ synth.bf16_bits_to_f32(b).astype(np.float64)
     err = rel_err(y, ref)
-    assert err <= NORTH_STAR_TOL
+    assert err <= REQUIRED_TOL
     assert err <= REL, err
     for x in bufs:
         session.free(x)
