@@ -138,4 +138,6 @@ cudaError_t fer_embed_f32(const int* tok, const void* emb, float* x, int T, int 
 cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* out, int T, int d, float eps,
                         cudaStream_t s);
 cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s);
+cudaError_t fer_attn_causal_ex(const void* qkv, void* out, int B, int S, int d, int heads, int flags, uint32_t* err,
+                               cudaStream_t s);
 }

@@ -237,7 +237,7 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
         const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
         run(2, 0.0, [&] { return fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st); });
         run(0, gq, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_qkv[l], m->qkv, nullptr, Ti, 3 * d, d, kEpiBF16, err, st); });
-        run(1, ga, [&] { return fer_attn_causal(m->qkv, m->att, B, Sq, d, static_cast<int>(c.heads), st); });
+        run(1, ga, [&] { return fer_attn_causal_ex(m->qkv, m->att, B, Sq, d, static_cast<int>(c.heads), 0, err, st); });
         run(0, go, [&] { return fer_gemm_bf16_tc_ex(m->att, W + m->off_o[l], m->x, m->x, Ti, d, d, kEpiResidF32, err, st); });
         run(2, 0.0, [&] { return fer_ln_bf16(m->x, g2, b2, m->a, Ti, d, c.eps, st); });
         run(0, g1f, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_w1[l], m->hid, nullptr, Ti, F, d, kEpiGeluBF16, err, st); });

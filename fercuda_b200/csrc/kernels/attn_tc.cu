@@ -1,0 +1,406 @@
+// Causal multi-head attention, head_dim 64, on the 5th-generation tensor
+// cores (tcgen05), straight out of the fused QKV activation.
+//
+// qkv: [B*S, 3*d] bf16 row-major (q | k | v; head h at columns h*64 of each
+// third); out: [B*S, d] bf16. S must be a multiple of 128.
+//
+// One CTA per (128-query tile, head, sequence), two CTAs per SM. Per key
+// block j (128 keys, j = 0 .. query tile):
+//   warp 0      TMA: Q once, K_j into a 2-deep ring, V_j into one buffer,
+//               all 128-byte swizzled [128 rows x 64 bf16] boxes
+//   warp 1      tcgen05.mma from one thread: S = Q K_j^T (M128 N128, f32 in
+//               tensor memory), then O_j = P_j V_j (M128 N64, K = 128 keys)
+//   warps 2..5  one query row per thread: scores from tensor memory
+//               (tcgen05.ld), causal mask on the diagonal block, running max
+//               in the log2 domain, p = 2^(s*scale - m) (ex2.approx), row sum
+//               in f32, P rounded to bf16 into swizzled shared memory (the
+//               A operand of the P.V MMA); O_j from tensor memory is folded
+//               into f32 registers, o = o * 2^(m_old - m) + O_j.
+// Finally o / l is rounded to bf16 and stored. The arithmetic is the same
+// online softmax as the mma.sync kernel in xfmr_kernels.cu (and the oracle's
+// exp(s - max) / sum with P rounded to bf16 before P.V).
+// Every wait is bounded (about one second): on timeout the kernel records an
+// error bit, stops, releases tensor memory and returns. No TMA multicast.
+#include "sm100_util.cuh"
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace {
+
+using namespace fer::dev;
+
+constexpr int TQ = 128;                   // queries per CTA
+constexpr int TK = 128;                   // keys per block
+constexpr int TILE_BYTES = 128 * 128;     // [128 rows x 64 bf16], 16 KiB
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = TILE_BYTES;         // two K buffers
+constexpr int OFF_V = 3 * TILE_BYTES;
+constexpr int OFF_P = 4 * TILE_BYTES;     // P: keys 0..63 at +0, keys 64..127 at +16 KiB
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024;
+constexpr int kThreads = 192;
+constexpr uint32_t TMEM_COLS = 256;       // S at columns [0, 128), O at [128, 192)
+constexpr uint32_t COL_O = 128;
+
+// kind::f16 instruction descriptors: f32 accumulate, bf16 A and B, M = 128.
+// S = Q K^T: A and B K-major, N = 128. O = P V: A K-major, B (V) N-major, N = 64.
+constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescPV =
+    (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+
+struct Bars {
+    uint64_t q_full;
+    uint64_t k_full[2];
+    uint64_t k_empty[2];
+    uint64_t v_full;
+    uint64_t v_empty;
+    uint64_t s_full;
+    uint64_t s_free;
+    uint64_t p_full;
+    uint64_t o_full;
+    uint64_t o_free;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle, version 1.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;
+    d |= 2ull << 61;
+    return d;
+}
+
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t u;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(u) : "f"(hi), "f"(lo));
+    return u;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
+// Whole-warp bounded wait: every lane polls, the warp agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_causal_tc(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out, int S, int d,
+                   float scale_log2, uint32_t* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ Bars bars;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_addr(smem);
+
+    const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);   // longest tiles first
+    const int h = blockIdx.y;
+    const int seq_row0 = static_cast<int>(blockIdx.z) * S;
+    const int n_k = qt + 1;                                                             // key blocks 0 .. qt
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars.q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars.k_full[i], 1);
+            mbar_init(&bars.k_empty[i], 1);
+        }
+        mbar_init(&bars.v_full, 1);
+        mbar_init(&bars.v_empty, 1);
+        mbar_init(&bars.s_full, 1);
+        mbar_init(&bars.s_free, 4);
+        mbar_init(&bars.p_full, 4);
+        mbar_init(&bars.o_full, 1);
+        mbar_init(&bars.o_free, 4);
+        bars.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(&bars.tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = bars.tmem_base;
+    volatile int* abort_flag = &bars.abort_flag;
+
+    if (warp == 0) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&bars.q_full, TILE_BYTES);
+            tma_load_2d(sbase + OFF_Q, &tm, h * 64, seq_row0 + qt * TQ, &bars.q_full);
+        }
+        __syncwarp();
+        for (int j = 0; j < n_k && !warp_flag(abort_flag); ++j) {
+            const int st = j & 1;
+            const uint32_t use = static_cast<uint32_t>(j >> 1);
+            if (!warp_wait(&bars.k_empty[st], (use & 1u) ^ 1u)) {
+                if (lane == 0) report(err, kErrTimeoutSync);
+                *abort_flag = 1;
+                break;
+            }
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&bars.k_full[st], TILE_BYTES);
+                tma_load_2d(sbase + OFF_K + st * TILE_BYTES, &tm, d + h * 64, seq_row0 + j * TK, &bars.k_full[st]);
+            }
+            __syncwarp();
+            if (!warp_wait(&bars.v_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u)) {
+                if (lane == 0) report(err, kErrTimeoutSync);
+                *abort_flag = 1;
+                break;
+            }
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&bars.v_full, TILE_BYTES);
+                tma_load_2d(sbase + OFF_V, &tm, 2 * d + h * 64, seq_row0 + j * TK, &bars.v_full);
+            }
+            __syncwarp();
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        bool ok = warp_wait(&bars.q_full, 0);
+        for (int j = 0; j < n_k && ok && !warp_flag(abort_flag); ++j) {
+            const int st = j & 1;
+            const uint32_t use = static_cast<uint32_t>(j >> 1);
+            const uint32_t ph = static_cast<uint32_t>(j) & 1u, prev = ph ^ 1u;
+            ok = warp_wait(&bars.k_full[st], use & 1u) && (j == 0 || warp_wait(&bars.s_free, prev));
+            if (!ok) break;
+            fence_after();
+            if (lane == 0) {
+                const uint32_t q = sbase + OFF_Q, k = sbase + OFF_K + st * TILE_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma(tmem, sdesc(q + kk * 32, 16, 1024), sdesc(k + kk * 32, 16, 1024), kIdescS, kk ? 1u : 0u);
+                commit(&bars.k_empty[st]);
+                commit(&bars.s_full);
+            }
+            __syncwarp();
+            ok = warp_wait(&bars.p_full, ph) && (j == 0 || warp_wait(&bars.o_free, prev)) && warp_wait(&bars.v_full, ph);
+            if (!ok) break;
+            fence_after();
+            if (lane == 0) {
+                const uint32_t p = sbase + OFF_P, v = sbase + OFF_V;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma(tmem + COL_O, sdesc(p + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024),
+                        sdesc(v + kk * 2048, TILE_BYTES, 1024), kIdescPV, kk ? 1u : 0u);
+                commit(&bars.v_empty);
+                commit(&bars.o_full);
+            }
+            __syncwarp();
+        }
+        if (!ok) {
+            if (lane == 0) report(err, kErrTimeoutLoad);
+            *abort_flag = 1;
+        }
+    } else {
+        // ---------------- softmax warps: one query row per thread
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;                      // row in the query tile
+        const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        float m = -INFINITY, l = 0.0f;
+        float o[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) o[i] = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < n_k; ++j) {
+            const uint32_t ph = static_cast<uint32_t>(j) & 1u;
+            if (warp_flag(abort_flag) || !warp_wait(&bars.s_full, ph)) {
+                ok = false;
+                break;
+            }
+            fence_after();
+            const bool diag = j == qt;
+            // pass 1: row max of the raw scores (masked keys excluded)
+            float smax = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                float v[32];
+                tmem_ld32(trow + c * 32, v);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const bool masked = diag && (c * 32 + e > r);
+                    smax = fmaxf(smax, masked ? -INFINITY : v[e]);
+                }
+            }
+            const float m_new = fmaxf(m, smax * scale_log2);
+            const float alpha = ex2(m - m_new);
+            // pass 2: p = 2^(s*scale - m_new), row sum, P (bf16) into shared memory
+            float sum = 0.0f;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                float v[32];
+                tmem_ld32(trow + c * 32, v);
+                uint32_t w[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const bool m0 = diag && (c * 32 + e > r), m1 = diag && (c * 32 + e + 1 > r);
+                    const float p0 = m0 ? 0.0f : ex2(fmaf(v[e], scale_log2, -m_new));
+                    const float p1 = m1 ? 0.0f : ex2(fmaf(v[e + 1], scale_log2, -m_new));
+                    sum += p0;
+                    sum += p1;
+                    w[e >> 1] = pack_bf16x2(p0, p1);
+                }
+                const uint32_t prow = sbase + OFF_P + (c >> 1) * TILE_BYTES + r * 128;
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    const int chunk = (c & 1) * 4 + q4;
+                    st_shared_v4(prow + ((chunk ^ (r & 7)) << 4), w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2],
+                                 w[4 * q4 + 3]);
+                }
+            }
+            l = l * alpha + sum;
+            m = m_new;
+            fence_proxy_async_smem();   // P is read by the tensor core (async proxy)
+            fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&bars.s_free);
+                mbar_arrive(&bars.p_full);
+            }
+            if (!warp_wait(&bars.o_full, ph)) {
+                ok = false;
+                break;
+            }
+            fence_after();
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float v[32];
+                tmem_ld32(trow + COL_O + c * 32, v);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha, v[e]);
+            }
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.o_free);
+        }
+        if (!ok) {
+            if (lane == 0) report(err, kErrTimeoutMma);
+            *abort_flag = 1;
+        } else {
+            const float inv = 1.0f / l;
+            uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(seq_row0 + qt * TQ + r) * d + h * 64);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint4 u;
+                u.x = pack_bf16x2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+                u.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+                u.z = pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+                u.w = pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+                dst[c] = u;
+            }
+        }
+    }
+
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+}  // namespace
+
+// Returns cudaErrorNotSupported (launching nothing) for shapes this kernel
+// does not take: head_dim != 64, S % 128 != 0, misaligned qkv / out.
+extern "C" cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int S, int d, int heads, uint32_t* err,
+                                          cudaStream_t stream) {
+    if (B <= 0 || S <= 0 || heads <= 0 || d != heads * 64 || (S % TQ) != 0) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(out)) & 15u) return cudaErrorNotSupported;
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    CUtensorMap tm;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(3) * d, static_cast<cuuint64_t>(B) * S};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(3) * d * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    if (fn(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorNotSupported;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(attn_causal_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const float scale_log2 = 1.4426950408889634f / 8.0f;   // log2(e) / sqrt(64)
+    const dim3 grid(S / TQ, heads, B);
+    attn_causal_tc<<<grid, kThreads, SMEM_BYTES, stream>>>(tm, static_cast<__nv_bfloat16*>(out), S, d, scale_log2,
+                                                           err);
+    return cudaGetLastError();
+}

@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer
         int it = 0;
-        for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        for (int t = blockIdx.x; t < num_tiles && !warp_flag(abort_flag); t += gridDim.x) {
             int mb, nb;
             tile_coords(t, num_m, num_n, &mb, &nb);
             for (int kt = 0; kt < num_k; ++kt, ++it) {
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (lane 0 issues)
         int it = 0, local = 0;
-        for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++local) {
+        for (int t = blockIdx.x; t < num_tiles && !warp_flag(abort_flag); t += gridDim.x, ++local) {
             const int buf = local & 1;
             const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
             if (!__all_sync(0xffffffffu, mbar_wait(&bars.acc_empty[buf], acc_ph ^ 1u))) {
@@ -293,8 +293,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
             const int buf = local & 1;
             const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
-            if (!__all_sync(0xffffffffu, mbar_wait(&bars.acc_full[buf], acc_ph)) || *abort_flag) {
-                if (lane == 0 && !*abort_flag) report(err, kErrTimeoutMma);
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&bars.acc_full[buf], acc_ph));
+            if (!got || warp_flag(abort_flag)) {
+                if (lane == 0 && !got) report(err, kErrTimeoutMma);
                 *abort_flag = 1;
                 break;
             }

@@ -93,6 +93,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// A shared flag read by a whole warp, agreed across its lanes (any lane that
+// sees it set makes it set for all), so the warp takes one branch.
+__device__ __forceinline__ bool warp_flag(volatile int* f) { return __any_sync(0xffffffffu, *f != 0); }
+
 __device__ __forceinline__ void report(uint32_t* err, uint32_t bits) {
     if (err) atomicOr(err, bits);
 }

@@ -359,10 +359,25 @@ extern "C" cudaError_t fer_ln_bf16(const float* x, const float* g, const float* 
 }
 
 // Causal attention for head_dim 64; B sequences of S tokens; qkv [B*S, 3d].
-extern "C" cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s) {
+extern "C" cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int S, int d, int heads, uint32_t* err,
+                                          cudaStream_t stream);
+
+// flags bit 0: use the mma.sync kernel even where the tcgen05 kernel
+// (attn_tc.cu: S a multiple of 128) applies. err: device error word for the
+// tcgen05 kernel's bounded waits (may be null).
+extern "C" cudaError_t fer_attn_causal_ex(const void* qkv, void* out, int B, int S, int d, int heads, int flags,
+                                          uint32_t* err, cudaStream_t s) {
     if (d != heads * HD || B <= 0 || S <= 0) return cudaErrorInvalidValue;
+    if (!(flags & 1)) {
+        const cudaError_t e = fer_attn_causal_tc(qkv, out, B, S, d, heads, err, s);
+        if (e != cudaErrorNotSupported) return e;
+    }
     const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
     const dim3 grid((S + AM - 1) / AM, heads, B);
     attn_causal<<<grid, kAttnThreads, 0, s>>>(static_cast<const bf16*>(qkv), static_cast<bf16*>(out), S, d, scale_log2);
     return cudaGetLastError();
+}
+
+extern "C" cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s) {
+    return fer_attn_causal_ex(qkv, out, B, S, d, heads, 0, nullptr, s);
 }
