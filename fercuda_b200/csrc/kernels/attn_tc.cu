@@ -14,8 +14,10 @@
 //               (tcgen05.ld), causal mask on the diagonal block, running max
 //               in the log2 domain, p = 2^(s*scale - m) (ex2.approx), row sum
 //               in f32, P rounded to bf16 into swizzled shared memory (the
-//               A operand of the P.V MMA); O_j from tensor memory is folded
-//               into f32 registers, o = o * 2^(m_old - m) + O_j.
+//               A operand of the P.V MMA). O accumulates in tensor memory
+//               across key blocks; when a row's max grows the softmax thread
+//               rescales its O row in place (tcgen05.ld / st) before the
+//               next P.V lands on it.
 // Finally o / l is rounded to bf16 and stored. The arithmetic is the same
 // online softmax as the mma.sync kernel in xfmr_kernels.cu (and the oracle's
 // exp(s - max) / sum with P rounded to bf16 before P.V).
@@ -61,7 +63,6 @@ struct Bars {
     uint64_t s_free;
     uint64_t p_full;
     uint64_t o_full;
-    uint64_t o_free;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -102,19 +103,43 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+// 64 consecutive f32 columns of this thread's TMEM lane; the wait is in the
+// same asm statement, so no use of the registers can be scheduled before it.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Stores 32 f32 columns to this thread's TMEM lane and waits for the store.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+        "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
+        "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
+        "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -164,7 +189,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_init(&bars.s_free, 4);
         mbar_init(&bars.p_full, 4);
         mbar_init(&bars.o_full, 1);
-        mbar_init(&bars.o_free, 4);
         bars.abort_flag = 0;
         fence_mbar_init();
     }
@@ -231,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 commit(&bars.s_full);
             }
             __syncwarp();
-            ok = warp_wait(&bars.p_full, ph) && (j == 0 || warp_wait(&bars.o_free, prev)) && warp_wait(&bars.v_full, ph);
+            ok = warp_wait(&bars.p_full, ph) && warp_wait(&bars.v_full, ph);
             if (!ok) break;
             fence_after();
             if (lane == 0) {
@@ -239,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma(tmem + COL_O, sdesc(p + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024),
-                        sdesc(v + kk * 2048, TILE_BYTES, 1024), kIdescPV, kk ? 1u : 0u);
+                        sdesc(v + kk * 2048, TILE_BYTES, 1024), kIdescPV, (j | kk) ? 1u : 0u);
                 commit(&bars.v_empty);
                 commit(&bars.o_full);
             }
@@ -255,9 +279,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int r = quarter * 32 + lane;                      // row in the query tile
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         float m = -INFINITY, l = 0.0f;
-        float o[64];
-#pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = 0.0f;
         bool ok = true;
         for (int j = 0; j < n_k; ++j) {
             const uint32_t ph = static_cast<uint32_t>(j) & 1u;
@@ -265,36 +286,43 @@ __global__ void __launch_bounds__(kThreads, 2)
                 ok = false;
                 break;
             }
-            fence_after();
-            const bool diag = j == qt;
-            // pass 1: row max of the raw scores (masked keys excluded)
-            float smax = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(trow + c * 32, v);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const bool masked = diag && (c * 32 + e > r);
-                    smax = fmaxf(smax, masked ? -INFINITY : v[e]);
-                }
+            // S_j's commit follows P_{j-1} V_{j-1} in issue order, so this
+            // wait returns at once; after it P's buffer and O are ours.
+            if (j > 0 && !warp_wait(&bars.o_full, ph ^ 1u)) {
+                ok = false;
+                break;
             }
+            fence_after();
+            float sv[128];
+            tmem_ld64(trow, sv);
+            tmem_ld64(trow + 64, sv + 64);
+            if (j == qt) {
+#pragma unroll
+                for (int e = 0; e < 128; ++e)
+                    if (e > r) sv[e] = -INFINITY;               // causal mask on the diagonal block
+            }
+            float mx[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mx[e] = sv[e];
+#pragma unroll
+            for (int e = 8; e < 128; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[e]);
+            const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             const float m_new = fmaxf(m, smax * scale_log2);
             const float alpha = ex2(m - m_new);
-            // pass 2: p = 2^(s*scale - m_new), row sum, P (bf16) into shared memory
-            float sum = 0.0f;
-#pragma unroll 1
+            // p = 2^(s*scale - m_new), row sum, P (bf16) into shared memory
+            float sm[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sm[e] = 0.0f;
+#pragma unroll
             for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(trow + c * 32, v);
                 uint32_t w[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    const bool m0 = diag && (c * 32 + e > r), m1 = diag && (c * 32 + e + 1 > r);
-                    const float p0 = m0 ? 0.0f : ex2(fmaf(v[e], scale_log2, -m_new));
-                    const float p1 = m1 ? 0.0f : ex2(fmaf(v[e + 1], scale_log2, -m_new));
-                    sum += p0;
-                    sum += p1;
+                    const float p0 = ex2(fmaf(sv[c * 32 + e], scale_log2, -m_new));
+                    const float p1 = ex2(fmaf(sv[c * 32 + e + 1], scale_log2, -m_new));
+                    sm[e & 7] += p0;
+                    sm[(e + 1) & 7] += p1;
                     w[e >> 1] = pack_bf16x2(p0, p1);
                 }
                 const uint32_t prow = sbase + OFF_P + (c >> 1) * TILE_BYTES + r * 128;
@@ -303,6 +331,19 @@ __global__ void __launch_bounds__(kThreads, 2)
                     const int chunk = (c & 1) * 4 + q4;
                     st_shared_v4(prow + ((chunk ^ (r & 7)) << 4), w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2],
                                  w[4 * q4 + 3]);
+                }
+            }
+            const float sum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+            // O holds sum_{i<j} P_i V_i scaled by 2^-m: rescale it in place
+            // before P_j V_j accumulates on it.
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+                for (int c = 0; c < 2; ++c) {
+                    float ov[32];
+                    tmem_ld32(trow + COL_O + c * 32, ov);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+                    tmem_st32(trow + COL_O + c * 32, ov);
                 }
             }
             l = l * alpha + sum;
@@ -314,26 +355,15 @@ __global__ void __launch_bounds__(kThreads, 2)
                 mbar_arrive(&bars.s_free);
                 mbar_arrive(&bars.p_full);
             }
-            if (!warp_wait(&bars.o_full, ph)) {
-                ok = false;
-                break;
-            }
-            fence_after();
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                tmem_ld32(trow + COL_O + c * 32, v);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(o[c * 32 + e], alpha, v[e]);
-            }
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars.o_free);
         }
+        if (ok && !warp_wait(&bars.o_full, static_cast<uint32_t>(n_k - 1) & 1u)) ok = false;
         if (!ok) {
             if (lane == 0) report(err, kErrTimeoutMma);
             *abort_flag = 1;
         } else {
+            fence_after();
+            float o[64];
+            tmem_ld64(trow + COL_O, o);
             const float inv = 1.0f / l;
             uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(seq_row0 + qt * TQ + r) * d + h * 64);
 #pragma unroll
