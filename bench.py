@@ -76,7 +76,7 @@ def host_threads() -> int:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 50 ms."""
+    """nvidia-smi clocks and throttle reasons sampled every 20 ms."""
 
     def __init__(self, index: int):
         self.index, self.samples, self.proc, self.t0, self.t1 = index, [], None, None, None
@@ -87,7 +87,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=subprocess.PIPE,
+                                          "--format=csv,noheader,nounits", "-lms", "20"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -343,7 +343,7 @@ class Gemm:
 
 class Transformer:
     """Decoder-only transformer forward, batch-sharded (fer_transformer_forward)."""
-    metric, unit, kernel = METRIC_TOK, "tokens/s", "gemm_tc_transformer"
+    metric, unit, kernel = METRIC_TOK, "tokens/s", "gemm_tc_transformer_b8"
 
     def __init__(self, s, capi, synth, rank=0, world=1, dist=None, torch=None, batch=None):
         cfg = dict(synth.TRANSFORMER)
@@ -416,6 +416,7 @@ class Transformer:
         per_launch = prof.gemm_flops / max(1, prof.forwards) / (4 * self.cfg["layers"] + 1)   # mean over the GEMMs
         return {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
                 "frac": round(ach / pk, 4), "traffic": profiled_traffic(self.kernel),
+                "traffic_note": "ncu DRAM bytes per GEMM launch, mean over the 33 GEMMs of a B=8 forward",
                 "algorithmic_flops_per_launch": round(per_launch), "peak_source": src + " (burst)",
                 "kernel": "gemm_bf16_tc_kernel (all GEMMs of the forward)",
                 "share_of_forward": round(prof.gemm_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4),
@@ -440,9 +441,13 @@ class Transformer:
         wbits = Transformer._cpu_w
         toks = np.minimum((synth.uniform01(c["token_seed"], seqs * c["seq"]) * c["vocab"]).astype(np.int32),
                           c["vocab"] - 1).reshape(seqs, c["seq"])
-        t0 = time.perf_counter()
-        ref.forward(toks, wbits, c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"], c["eps"])
-        dt = time.perf_counter() - t0
+        from threadpoolctl import threadpool_limits
+
+        # torchrun sets OMP_NUM_THREADS=1 per rank; the CPU leg uses every host thread
+        with threadpool_limits(limits=threads):
+            t0 = time.perf_counter()
+            ref.forward(toks, wbits, c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"], c["eps"])
+            dt = time.perf_counter() - t0
         return seqs * c["seq"] / dt, f"{seqs} sequence(s) x 512 tokens through the numpy restatement", threads
 
 
