@@ -374,6 +374,285 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ================================================================ 2-CTA version
+//
+// A cluster of two CTAs (two SMs) computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256): CTA r holds A rows [128r, 128r+128) of
+// the tile and B columns [128r, 128r+128), so each SM fetches 32 KiB per
+// 64-deep k-block instead of 48 KiB, and six stages fit where four did.
+// Both CTAs' TMA loads complete on the leader's (rank 0) full barrier; the
+// leader's MMA thread issues for the pair and its commits arrive on both
+// CTAs' barriers (tcgen05.commit multicast). Each CTA's epilogue drains its
+// own TMEM rows (same code path as above) and releases the accumulator with
+// an arrive on the leader's acc_empty barrier. No TMA multicast is used.
+constexpr int STAGES2 = 6;
+constexpr int A2_BYTES = 128 * BK * 2;            // 16 KiB: this CTA's 128 rows
+constexpr int B2_BYTES = BK * 128 * 2;            // 16 KiB: this CTA's 128 columns (two 64-column panels)
+constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + EPI_WARPS * STAGING_BYTES + 1024;
+constexpr int GROUP_M2 = 8;                       // 256-row blocks per raster group
+// kind::f16, f32 accumulator, bf16 A/B, A K-major, B N-major, N = 256, M = 256.
+constexpr uint32_t kIdesc2 = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (static_cast<uint32_t>(256 >> 3) << 17) |
+                             (static_cast<uint32_t>(256 >> 4) << 24);
+
+struct Bars2 {
+    uint64_t full[STAGES2];     // leader's copy is the one used
+    uint64_t empty[STAGES2];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];      // leader's copy: 2 x EPI_WARPS arrivals per phase
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t nclusters_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc2), "r"(accumulate)
+        : "memory");
+}
+// Arrives on the barrier at this offset in both CTAs once the MMAs issued so far complete.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_addr(bar)),
+        "h"(static_cast<uint16_t>(3))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__device__ __forceinline__ void tile_coords2(int t, int num_m2, int num_n, int* mb, int* nb) {
+    const int per_group = GROUP_M2 * num_n;
+    const int g = t / per_group;
+    const int first_m = g * GROUP_M2;
+    const int gm = (num_m2 - first_m) < GROUP_M2 ? (num_m2 - first_m) : GROUP_M2;
+    const int r = t - g * per_group;
+    *mb = first_m + r % gm;
+    *nb = r / gm;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, uint32_t* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ Bars2 bars;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int cid = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(nclusters_x());
+    const int num_m2 = (M + 255) / 256, num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m2 * num_n;
+    const int num_k = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES2; ++s) {
+            mbar_init(&bars.full[s], 1);
+            mbar_init(&bars.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars.acc_full[b], 1);
+            mbar_init(&bars.acc_empty[b], 2 * EPI_WARPS);
+        }
+        bars.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bars.tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync_all();   // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem = bars.tmem_base;
+    volatile int* abort_flag = &bars.abort_flag;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs): own A rows, own B columns
+        const uint32_t full0 = map_to_rank(smem_addr(&bars.full[0]), 0);
+        int it = 0;
+        for (int t = cid; t < num_tiles && !warp_flag(abort_flag); t += ncl) {
+            int mb, nb;
+            tile_coords2(t, num_m2, num_n, &mb, &nb);
+            const int row = mb * 256 + static_cast<int>(rank) * 128;
+            const int col = nb * BN + static_cast<int>(rank) * 128;
+            for (int kt = 0; kt < num_k; ++kt, ++it) {
+                const int s = it % STAGES2;
+                const uint32_t ph = static_cast<uint32_t>(it / STAGES2) & 1u;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars.empty[s], ph ^ 1u))) {
+                    if (lane == 0) report(err, kErrTimeoutSync);
+                    *abort_flag = 1;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fb = full0 + static_cast<uint32_t>(s * sizeof(uint64_t));
+                    if (leader) mbar_arrive_expect_tx(&bars.full[s], 2 * STAGE2_BYTES);
+                    const uint32_t sa = smem_addr(smem + s * STAGE2_BYTES);
+                    tma_load_2d_pair(sa, &tmA, kt * BK, row, fb);
+                    tma_load_2d_pair(sa + A2_BYTES, &tmB, col, kt * BK, fb);
+                    tma_load_2d_pair(sa + A2_BYTES + BK * 128, &tmB, col + 64, kt * BK, fb);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: the leader's warp 1 issues for the pair
+        if (leader) {
+            int it = 0, local = 0;
+            for (int t = cid; t < num_tiles && !warp_flag(abort_flag); t += ncl, ++local) {
+                const int buf = local & 1;
+                const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars.acc_empty[buf], acc_ph ^ 1u))) {
+                    if (lane == 0) report(err, kErrTimeoutSync);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+                bool ok = true;
+                for (int kt = 0; kt < num_k; ++kt, ++it) {
+                    const int s = it % STAGES2;
+                    const uint32_t ph = static_cast<uint32_t>(it / STAGES2) & 1u;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&bars.full[s], ph))) {
+                        if (lane == 0) report(err, kErrTimeoutLoad);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t sa = smem_addr(smem + s * STAGE2_BYTES);
+                        const uint32_t sb = sa + A2_BYTES;
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k) {
+                            const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
+                            const uint64_t bd = smem_desc(sb + k * 16 * 128, BK * 128, 1024);
+                            mma_bf16_pair(d, ad, bd, (kt | k) ? 1u : 0u);
+                        }
+                        mma_commit_pair(&bars.empty[s]);
+                    }
+                    __syncwarp();
+                }
+                if (!ok) break;
+                if (lane == 0) mma_commit_pair(&bars.acc_full[buf]);
+                __syncwarp();
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..9 (both CTAs): this CTA's 128 rows
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const uint32_t stage = smem_addr(smem + STAGES2 * STAGE2_BYTES + (warp - 2) * STAGING_BYTES);
+        const uint32_t acc_empty0 = map_to_rank(smem_addr(&bars.acc_empty[0]), 0);
+        const bool f32_out = epi == kEpiF32 || epi == kEpiResidF32;
+        const int chunk_cols = f32_out ? 32 : 64;
+        const int n_chunks = (BN / 2) / chunk_cols;
+        int local = 0;
+        for (int t = cid; t < num_tiles; t += ncl, ++local) {
+            const int buf = local & 1;
+            const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&bars.acc_full[buf], acc_ph));
+            if (!got || warp_flag(abort_flag)) {
+                if (lane == 0 && !got) report(err, kErrTimeoutMma);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            int mb, nb;
+            tile_coords2(t, num_m2, num_n, &mb, &nb);
+            const int row0 = mb * 256 + static_cast<int>(rank) * 128 + q * 32;
+            const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(buf * BN + half * (BN / 2));
+#pragma unroll 1
+            for (int c = 0; c < n_chunks; ++c) {
+                uint32_t w[32];
+                if (f32_out) {
+                    tmem_ld32(tbase + c * 32, w);
+                } else {
+                    const bool gelu = epi == kEpiGeluBF16;
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 64 + h2 * 32, r);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            float a0 = __uint_as_float(r[2 * j]), a1 = __uint_as_float(r[2 * j + 1]);
+                            if (gelu) {
+                                a0 = gelu_erf(a0);
+                                a1 = gelu_erf(a1);
+                            }
+                            w[16 * h2 + j] = pack_bf16x2(a0, a1);
+                        }
+                    }
+                }
+                if (c == n_chunks - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc_empty0 + static_cast<uint32_t>(buf * sizeof(uint64_t)));
+                }
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+                stage_row(stage, lane, w);
+                fence_proxy_async_smem();
+                __syncwarp();
+                const int col0 = nb * BN + half * (BN / 2) + c * chunk_cols;
+                if (lane == 0 && row0 < M && col0 < N) {
+                    if (epi == kEpiResidF32) tma_reduce_add_2d(&tmC, stage, col0, row0);
+                    else tma_store_2d(&tmC, stage, col0, row0);
+                    bulk_commit();
+                }
+                __syncwarp();
+            }
+        }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    cluster_sync_all();   // no CTA leaves while its peer's MMAs or arrivals may still touch it
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
 // ---------------------------------------------------------------- host side
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -420,7 +699,18 @@ int sm_count() {
     return n;
 }
 
+int g_gemm_mode = 0;        // 0: 2-CTA kernel where it applies, 1: always the 1-CTA kernel
+int g_gemm_clusters = -1;   // co-resident 2-CTA clusters (queried once)
+
 }  // namespace
+
+// Selects the GEMM kernel: 0 (default) the 2-CTA cluster kernel for M > 128,
+// 1 the single-CTA kernel everywhere. Both give bit-identical results.
+extern "C" void fer_gemm_tc_set_mode(int mode) { g_gemm_mode = mode; }
+
+// Number of 2-CTA clusters the persistent kernel launches at most (-1 before
+// the first 2-CTA GEMM on this device).
+extern "C" int fer_gemm_tc_clusters() { return g_gemm_clusters; }
 
 // epi: 0 f32 out, 1 bf16 out, 2 bf16(gelu(acc)), 3 f32 out = resid + acc.
 // With resid == c the residual add happens in place (TMA reduce-add); any
@@ -447,6 +737,29 @@ extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c
         if (r0 < c0 + bytes && c0 < r0 + bytes) return cudaErrorInvalidValue;
         cudaError_t e = cudaMemcpyAsync(c, resid, bytes, cudaMemcpyDeviceToDevice, stream);
         if (e != cudaSuccess) return e;
+    }
+    if (g_gemm_mode != 1 && M > BM) {
+        // 2-CTA kernel: A boxes of 128 rows per CTA, one 256-row tile per cluster
+        int& clusters = g_gemm_clusters;
+        if (clusters < 0) {
+            cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 SMEM2_BYTES);
+            if (e != cudaSuccess) return e;
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = SMEM2_BYTES;
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tc2_kernel, &cfg);
+            clusters = (e == cudaSuccess && n > 0) ? n : 0;
+            if (e != cudaSuccess) cudaGetLastError();
+        }
+        if (clusters > 0) {
+            const int tiles2 = ((M + 255) / 256) * ((N + BN - 1) / BN);
+            const int ncl = tiles2 < clusters ? tiles2 : clusters;
+            gemm_bf16_tc2_kernel<<<2 * ncl, kThreads, SMEM2_BYTES, stream>>>(ma, mb, mc, M, N, K, epi, err);
+            return cudaGetLastError();
+        }
     }
     static bool attr_set = false;
     if (!attr_set) {

@@ -122,3 +122,29 @@ def test_partial_overlap_rejected():
     rc = kern().fer_gemm_bf16_tc_ex(ta.data_ptr(), tb.data_ptr(), buf.data_ptr(), buf[256:].data_ptr(), m, n, k,
                                     EPI_RESID, None, torch.cuda.current_stream().cuda_stream)
     assert rc != 0
+
+
+@pytest.mark.parametrize("m,n,k,epi", [(300, 200, 192, EPI_F32), (1024, 3072, 1024, EPI_BF16), (517, 648, 1000, EPI_GELU),
+                                       (640, 1024, 4096, EPI_RESID), (129, 256, 64, EPI_F32)])
+def test_two_cta_kernel_matches_single_cta_kernel(m, n, k, epi):
+    """The default 2-CTA cluster kernel (M > 128) against the single-CTA
+    kernel on the same operands: same K order per output, so the same bits."""
+    a, b = operands(m, n, k, 71)
+    dt = torch.float32 if epi in (EPI_F32, EPI_RESID) else torch.bfloat16
+    x0 = torch.from_numpy(synth.normal_f32(72, m * n).reshape(m, n)).cuda()
+    outs = []
+    k_ = kern()
+    k_.fer_gemm_tc_set_mode.argtypes = [C.c_int]
+    try:
+        for mode in (0, 1):
+            k_.fer_gemm_tc_set_mode(mode)
+            out = x0.clone() if epi == EPI_RESID else torch.empty(m, n, dtype=dt, device="cuda")
+            outs.append(launch(a, b, out, out if epi == EPI_RESID else None, m, n, k, epi))
+    finally:
+        k_.fer_gemm_tc_set_mode(0)
+    ref = f64(a) @ f64(b) + (x0.double().cpu().numpy() if epi == EPI_RESID else 0.0)
+    if epi == EPI_GELU:
+        ref = 0.5 * ref * (1.0 + erf(ref / np.sqrt(2.0)))
+    y = outs[0].float().cpu().numpy()
+    assert np.abs(y - ref).max() <= (2.0 ** -7 if dt == torch.bfloat16 else REL) * np.abs(ref).max() + REL
+    assert torch.equal(outs[0], outs[1])
