@@ -129,10 +129,13 @@ class ClockSampler:
 
 class Rows:
     """Row softmax -> layer norm, f32 [4096, 4096] (fer_submit_rows)."""
-    metric, unit, kernel = METRIC_HBM, "GB/s", "rows_softmax_layernorm_4096x4096"
+    metric, unit, kernel = METRIC_HBM, "GB/s", "rows_fast_softmax_layernorm_4096x4096"
+    exact = False
 
-    def __init__(self, s, capi, synth, rows=4096, cols=4096):
+    def __init__(self, s, capi, synth, rows=4096, cols=4096, exact=False):
         self.s, self.capi, self.rows, self.cols = s, capi, rows, cols
+        self.exact = exact
+        self.kernel = "rows_softmax_layernorm_4096x4096" if exact else "rows_fast_softmax_layernorm_4096x4096"
         self.eps = synth.SOFTMAX_LAYERNORM["eps"]
         self.x = synth.softmax_layernorm_input(rows, cols)
         self.pairs = []
@@ -140,8 +143,8 @@ class Rows:
             bx, by = s.alloc(capi.FER_DTYPE_F32, [rows, cols]), s.alloc(capi.FER_DTYPE_F32, [rows, cols])
             s.upload(bx, self.x)
             self.pairs.append((bx, by))
-        self.req = [capi.fer_rows_request_t(bx, by, 0, 0, self.eps, capi.FER_ROWS_SOFTMAX | capi.FER_ROWS_LAYER_NORM,
-                                            capi.FER_MEMORY_AUTO) for bx, by in self.pairs]
+        ops = capi.FER_ROWS_SOFTMAX | capi.FER_ROWS_LAYER_NORM | (0 if exact else capi.FER_ROWS_FAST)
+        self.req = [capi.fer_rows_request_t(bx, by, 0, 0, self.eps, ops, capi.FER_MEMORY_AUTO) for bx, by in self.pairs]
         self.job = C.c_uint64()
         self.units_per_step = 8 * rows * cols           # algorithmic bytes
         self.launches_per_step = 1
@@ -154,13 +157,18 @@ class Rows:
             raise RuntimeError(st.message)
 
     def config(self, world):
-        return self.describe(world)
+        c = self.describe(world)
+        if self.exact:
+            c["path"] = "reference order (bit-identical to the reference kernels)"
+            c["api"] = "fer_submit_rows (SOFTMAX|LAYER_NORM)"
+        return c
 
     @staticmethod
     def describe(world, rows=4096, cols=4096):
         return {"workload": f"softmax_layernorm_{rows}x{cols}_f32", "rows": rows, "cols": cols,
+                "path": "fast deterministic (<= 1e-5 of the reference order, bit-identical run to run)",
                 "eps": 1e-5, "gamma": 1.0, "beta": 0.0, "input": "N(0,1) seed 1",
-                "l2": "rotating 3 input/output pairs (384 MiB > 126 MB L2)", "api": "fer_submit_rows",
+                "l2": "rotating 3 input/output pairs (384 MiB > 126 MB L2)", "api": "fer_submit_rows (SOFTMAX|LAYER_NORM|FAST)",
                 "parallelism": f"replicas x{world}"}
 
     def e2e_prepare(self, torch):
@@ -176,9 +184,10 @@ class Rows:
     def roofline(self, kern_ms):
         pk, src = peak("hbm_gbs")
         ach = self.units_per_step / (kern_ms * 1e-3) / 1e9
+        kernel = "rows_bulk_kernel" if getattr(self, "exact", True) else "rows_fast_kernel"
         return {"bound": "hbm", "achieved": round(ach, 1), "peak": pk, "unit": "GB/s", "frac": round(ach / pk, 4),
                 "traffic": profiled_traffic(self.kernel), "algorithmic_bytes_per_launch": self.units_per_step,
-                "peak_source": pk and src, "kernel": "rows_bulk_kernel", "kernel_ms_median": round(kern_ms, 5)}
+                "peak_source": src, "kernel": kernel, "kernel_ms_median": round(kern_ms, 5)}
 
     @staticmethod
     def cpu(threads, reps=3):
@@ -588,8 +597,9 @@ def max_over_ranks(v, torch, dist, world):
 def subresults(s, capi, synth, torch, stream):
     """Short measurements of the other workloads (one GPU)."""
     out = {}
-    for name, cls, steps in (("softmax_layernorm", Rows, 50), ("fused_elementwise", Chain, 200), ("gemm", Gemm, 10)):
-        wl = cls(s, capi, synth)
+    for name, cls, steps in (("softmax_layernorm", Rows, 50), ("softmax_layernorm_reference_order", Rows, 50),
+                             ("fused_elementwise", Chain, 200), ("gemm", Gemm, 10)):
+        wl = cls(s, capi, synth, exact=True) if name == "softmax_layernorm_reference_order" else cls(s, capi, synth)
         el, kern = timed_steps(wl, torch, stream, steps, 5, None, 1)
         med = float(np.median(kern))
         unit_scale = 1e9 if cls is not Gemm else 1e12

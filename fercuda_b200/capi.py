@@ -42,7 +42,7 @@ FER_JIT_INTENT_FUSION_NONE = 0
 FER_JIT_INTENT_FUSION_RELU = 1
 FER_JIT_INTENT_FUSION_MUL_SIGMOID_INPUT = 2
 
-FER_ROWS_SOFTMAX, FER_ROWS_LAYER_NORM = 1, 2
+FER_ROWS_SOFTMAX, FER_ROWS_LAYER_NORM, FER_ROWS_FAST = 1, 2, 4
 (FER_CHAIN_LOAD, FER_CHAIN_AFFINE, FER_CHAIN_ADD_SCALAR, FER_CHAIN_MUL_SCALAR, FER_CHAIN_RELU, FER_CHAIN_SIGMOID,
  FER_CHAIN_EXP, FER_CHAIN_TANH, FER_CHAIN_GELU_TANH, FER_CHAIN_SILU, FER_CHAIN_NEG, FER_CHAIN_ABS, FER_CHAIN_CLAMP,
  FER_CHAIN_ADD, FER_CHAIN_SUB, FER_CHAIN_MUL, FER_CHAIN_DIV, FER_CHAIN_MAX, FER_CHAIN_MIN, FER_CHAIN_RELU_LT,

@@ -120,7 +120,9 @@ fer_status_t fer_submit_rows(fer_session_t* session, const fer_rows_request_t* r
     if (!x || !o) return not_found("buffer id not found");
     if (x->desc.dtype != FER_DTYPE_F32 || o->desc.dtype != FER_DTYPE_F32) return invalid("rows requires f32 buffers");
     if (x->desc.rank > 2 || o->numel != x->numel) return invalid("rows requires matching rank-1/2 buffers");
-    if (req->ops == 0 || (req->ops & ~(FER_ROWS_SOFTMAX | FER_ROWS_LAYER_NORM))) return invalid("rows ops must be SOFTMAX and/or LAYER_NORM");
+    const uint32_t ops = req->ops & (FER_ROWS_SOFTMAX | FER_ROWS_LAYER_NORM);
+    if (ops == 0 || (req->ops & ~(FER_ROWS_SOFTMAX | FER_ROWS_LAYER_NORM | FER_ROWS_FAST)))
+        return invalid("rows ops must be SOFTMAX and/or LAYER_NORM (optionally FAST)");
     const int rows = x->desc.rank == 2 ? static_cast<int>(x->desc.dims[0]) : 1;
     const int cols = x->desc.rank == 2 ? static_cast<int>(x->desc.dims[1]) : static_cast<int>(x->desc.dims[0]);
     const float* gamma = nullptr;
@@ -134,8 +136,14 @@ fer_status_t fer_submit_rows(fer_session_t* session, const fer_rows_request_t* r
             return invalid("gamma/beta must be f32 with cols elements");
         (k == 0 ? gamma : beta) = static_cast<const float*>(g->ptr);
     }
-    fer_status_t st = launched(fer_rows_f32(static_cast<const float*>(x->ptr), static_cast<float*>(o->ptr), gamma, beta,
-                                            rows, cols, req->eps, req->ops, S.dev_err, S.stream));
+    cudaError_t e = cudaErrorNotSupported;
+    if (req->ops & FER_ROWS_FAST)
+        e = fer_rows_fast_f32(static_cast<const float*>(x->ptr), static_cast<float*>(o->ptr), gamma, beta, rows, cols,
+                              req->eps, ops, S.dev_err, S.stream);
+    if (e == cudaErrorNotSupported)
+        e = fer_rows_f32(static_cast<const float*>(x->ptr), static_cast<float*>(o->ptr), gamma, beta, rows, cols,
+                         req->eps, ops, S.dev_err, S.stream);
+    fer_status_t st = launched(e);
     if (st.code != FER_STATUS_OK) return st;
     uint64_t job = 0;
     st = S.make_job({}, &job);

@@ -137,6 +137,8 @@ cudaError_t fer_embed_f32(const int* tok, const void* emb, float* x, int T, int 
                           cudaStream_t s);
 cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* out, int T, int d, float eps,
                         cudaStream_t s);
+cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
+                              float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s);
 cudaError_t fer_attn_causal_ex(const void* qkv, void* out, int B, int S, int d, int heads, int flags, uint32_t* err,
                                cudaStream_t s);

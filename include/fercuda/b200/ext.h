@@ -17,11 +17,16 @@ extern "C" {
 /* ---- row kernels ----------------------------------------------------------
  * Row softmax, row layer norm, or softmax followed by layer norm over a
  * rank-2 f32 buffer [rows, cols] (rank 1 = one row), in one fused pass.
- * Numerics match the reference's ptx_tensor_softmax_f32 and
+ * By default numerics match the reference's ptx_tensor_softmax_f32 and
  * fer_submit_layer_norm applied row by row, bit for bit.
+ * FER_ROWS_FAST selects a one-pass path with 128-bit accesses and an SFU
+ * exponential: bit-identical run to run, within 1e-5 (of the largest output)
+ * of the reference order; shapes it does not take (cols % 4 != 0,
+ * cols > 8192, in place, unaligned) run the reference-order path.
  * gamma / beta: optional rank-1 f32 [cols] buffers (0 = none). */
 #define FER_ROWS_SOFTMAX 1u
 #define FER_ROWS_LAYER_NORM 2u
+#define FER_ROWS_FAST 4u
 
 typedef struct fer_rows_request {
     uint64_t x;

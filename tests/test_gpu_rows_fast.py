@@ -1,0 +1,85 @@
+"""Fast deterministic row path (fer_submit_rows with FER_ROWS_FAST) on the GPU.
+
+The required bar for row reductions: max |ours - oracle| / max |oracle| <=
+TOL = 1e-5 against the reference order, and bit-identical outputs run to
+run. The fast path reorders the additions (vector chunks, xor-butterfly) and
+uses the SFU exponential, so it is held to that bar rather than to bit
+equality; shapes it does not take fall back to the reference-order path,
+which is bit-exact.
+"""
+import numpy as np
+import pytest
+
+from fercuda_b200 import capi, synth
+from tests import oracle_lib
+
+pytestmark = pytest.mark.gpu
+
+SM, LN, FAST = capi.FER_ROWS_SOFTMAX, capi.FER_ROWS_LAYER_NORM, capi.FER_ROWS_FAST
+EPS = 1e-5
+TOL = 1e-5
+
+
+def run(session, x, ops, gamma=None, beta=None):
+    rows, cols = x.shape
+    bx = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    by = session.alloc(capi.FER_DTYPE_F32, [rows, cols])
+    session.upload(bx, x)
+    ids = []
+    for arr in (gamma, beta):
+        if arr is None:
+            ids.append(0)
+            continue
+        b = session.alloc(capi.FER_DTYPE_F32, [cols])
+        session.upload(b, arr)
+        ids.append(b)
+    session.wait(session.rows(bx, by, ops, EPS, ids[0], ids[1]))
+    y = np.empty_like(x)
+    session.download(by, y)
+    for b in [bx, by] + [i for i in ids if i]:
+        session.free(b)
+    assert session.device_errors() == 0
+    return y
+
+
+def rel(y, ref):
+    return float(np.abs(y.astype(np.float64) - ref).max() / np.abs(ref).max())
+
+
+def test_config2_full_size_vs_oracle_and_deterministic(session):
+    x = synth.softmax_layernorm_input()
+    rows, cols = x.shape
+    ref = np.empty_like(x)
+    oracle_lib.load().orc_softmax_layernorm_rows_f32(oracle_lib.ptr(x), oracle_lib.ptr(ref), rows, cols, EPS, 8)
+    y1 = run(session, x, SM | LN | FAST)
+    assert rel(y1, ref) <= TOL
+    for _ in range(2):
+        y2 = run(session, x, SM | LN | FAST)
+        assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (7, 1000), (5, 256), (3, 8192), (9, 2052), (600, 512), (2, 4)])
+@pytest.mark.parametrize("ops", [SM | LN, SM, LN])
+def test_fast_vs_reference_order_path(session, rows, cols, ops):
+    x = synth.normal_f32(11 + cols, rows * cols, 0.0, 2.0).reshape(rows, cols)
+    exact = run(session, x, ops)
+    fast = run(session, x, ops | FAST)
+    assert rel(fast, exact.astype(np.float64)) <= TOL
+
+
+def test_fast_gamma_beta(session):
+    rows, cols = 33, 4096
+    x = synth.normal_f32(7, rows * cols).reshape(rows, cols)
+    g = synth.normal_f32(8, cols, 1.0, 0.1)
+    b = synth.normal_f32(9, cols, 0.0, 0.1)
+    exact = run(session, x, SM | LN, g, b)
+    fast = run(session, x, SM | LN | FAST, g, b)
+    assert rel(fast, exact.astype(np.float64)) <= TOL
+
+
+@pytest.mark.parametrize("rows,cols", [(3, 102), (2, 16384), (4, 1002)])
+def test_unsupported_shapes_take_the_reference_order_path(session, rows, cols):
+    x = synth.normal_f32(13, rows * cols).reshape(rows, cols)
+    exact = run(session, x, SM | LN)
+    fast = run(session, x, SM | LN | FAST)
+    assert np.array_equal(exact.view(np.uint32), fast.view(np.uint32))
