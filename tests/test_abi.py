@@ -16,7 +16,7 @@ HEADERS = {
     "libfercuda_capi.so": ["include/fercuda/api/c_api.h", "include/fercuda/jit/api.h",
                            "include/fercuda/jit/intent/intent.h", "include/fercuda/b200/ext.h"],
     "libptx_core.so": ["include/ptx/memory/ptx_tlsf_allocator.h", "include/ptx/gpu/gpu_hot_runtime.h"],
-    "libptx_kernels.so": ["include/ptx/gpu/tensor_ops.h"],
+    "libptx_kernels.so": ["include/ptx/gpu/tensor_ops.h", "include/fercuda/b200/native.h"],
 }
 REFERENCE = Path("/root/reference")
 
