@@ -187,7 +187,7 @@ class Rows:
         kernel = "rows_bulk_kernel" if getattr(self, "exact", True) else "rows_fast_kernel"
         return {"bound": "hbm", "achieved": round(ach, 1), "peak": pk, "unit": "GB/s", "frac": round(ach / pk, 4),
                 "traffic": profiled_traffic(self.kernel), "algorithmic_bytes_per_launch": self.units_per_step,
-                "peak_source": src, "kernel": kernel, "kernel_ms_median": round(kern_ms, 5)}
+                "peak_source": src, "kernel": kernel, "kernel_ms_per_launch": round(kern_ms, 5)}
 
     @staticmethod
     def cpu(threads, reps=3):
@@ -270,7 +270,7 @@ class Chain(Rows):
 
 class Gemm:
     """bf16 8192^3 -> f32, deterministic tcgen05 GEMM (fer_submit_gemm)."""
-    metric, unit, kernel = "deterministic GEMM TFLOP/s (bf16 in, f32 accumulate)", "TFLOP/s", "gemm_tc_8192"
+    metric, unit, kernel = "deterministic GEMM TFLOP/s (bf16 in, f32 accumulate)", "TFLOP/s", "gemm_tc2_8192"
 
     def __init__(self, s, capi, synth, m=8192, n=8192, k=8192):
         self.s, self.capi, self.m, self.n, self.k = s, capi, m, n, k
@@ -325,7 +325,8 @@ class Gemm:
         ach = self.units_per_step / (kern_ms * 1e-3) / 1e12
         return {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s", "frac": round(ach / pk, 4),
                 "traffic": profiled_traffic(self.kernel), "algorithmic_flops_per_launch": self.units_per_step,
-                "peak_source": src + " (burst)", "kernel": "gemm_bf16_tc_kernel", "kernel_ms_median": round(kern_ms, 5)}
+                "peak_source": src + " (burst)", "kernel": "gemm_bf16_tc2_kernel (2-CTA clusters)",
+                "kernel_ms_per_launch": round(kern_ms, 5)}
 
     @staticmethod
     def cpu(threads, tiles=4):
@@ -427,7 +428,7 @@ class Transformer:
                 "frac": round(ach / pk, 4), "traffic": profiled_traffic(self.kernel),
                 "traffic_note": "ncu DRAM bytes per GEMM launch, mean over the 33 GEMMs of a B=8 forward",
                 "algorithmic_flops_per_launch": round(per_launch), "peak_source": src + " (burst)",
-                "kernel": "gemm_bf16_tc_kernel (all GEMMs of the forward)",
+                "kernel": "gemm_bf16_tc2_kernel (all GEMMs of the forward)",
                 "share_of_forward": round(prof.gemm_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4),
                 "attention_tflops": round(prof.attn_flops / (prof.attn_ms * 1e-3) / 1e12, 1) if prof.attn_ms else None,
                 "attention_share": round(prof.attn_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4),
@@ -562,32 +563,29 @@ WORKLOADS = {"transformer": Transformer, "softmax_layernorm": Rows, "fused_eleme
 # ================================================================ runners
 
 
-def timed_steps(wl, torch, stream, steps, warmup, dist, world, per_launch=True):
+def timed_steps(wl, torch, stream, steps, warmup, dist, world):
+    """W warm-up steps, then exactly `steps` steps between one pair of CUDA
+    events on the session stream (barrier + synchronize on both sides).
+    Returns the elapsed milliseconds; elapsed / steps is the average launch
+    duration of a one-kernel step (host-side events per launch would make
+    short kernels host-bound and are not recorded)."""
     for i in range(warmup):
         wl.step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)] if per_launch else []
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)] if per_launch else []
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0.record(stream)
     for i in range(steps):
-        if per_launch:
-            starts[i].record(stream)
         wl.step(warmup + i)
-        if per_launch:
-            ends[i].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    elapsed = t0.elapsed_time(t1)
-    kern = [a.elapsed_time(b) for a, b in zip(starts, ends)]
-    return elapsed, kern
+    return t0.elapsed_time(t1)
 
 
 def max_over_ranks(v, torch, dist, world):
@@ -600,8 +598,8 @@ def subresults(s, capi, synth, torch, stream):
     for name, cls, steps in (("softmax_layernorm", Rows, 50), ("softmax_layernorm_reference_order", Rows, 50),
                              ("fused_elementwise", Chain, 200), ("gemm", Gemm, 10)):
         wl = cls(s, capi, synth, exact=True) if name == "softmax_layernorm_reference_order" else cls(s, capi, synth)
-        el, kern = timed_steps(wl, torch, stream, steps, 5, None, 1)
-        med = float(np.median(kern))
+        el = timed_steps(wl, torch, stream, steps, 5, None, 1)
+        med = el / steps
         unit_scale = 1e9 if cls is not Gemm else 1e12
         out[name] = {"metric": cls.metric, "value": round(wl.units_per_step * steps / (el * 1e-3) / unit_scale, 2),
                      "unit": cls.unit, "steps": steps, "config": wl.config(1), "roofline": wl.roofline(med),
@@ -733,8 +731,7 @@ def main():
     clocks.start()
     time.sleep(0.25)
     clocks.mark(True)
-    elapsed, kern = timed_steps(wl, torch, stream, args.steps, args.warmup, dist, world,
-                                per_launch=cls is not Transformer)
+    elapsed = timed_steps(wl, torch, stream, args.steps, args.warmup, dist, world)
     clocks.mark(False)
     clk = clocks.stop()
     elapsed = max_over_ranks(elapsed, torch, dist, world)
@@ -772,7 +769,7 @@ def main():
             unit_scale = 1e12 if cls is Gemm else 1e9
             value = wl.units_per_step * args.steps * world / (elapsed * 1e-3) / unit_scale
             e2e_v = wl.units_per_step * e2e_steps * world / e2e_s / unit_scale
-            roof = wl.roofline(float(np.median(kern)))
+            roof = wl.roofline(elapsed / args.steps)
             launches = wl.launches_per_step * args.steps
         cpu_base = None
         if world == 1:
