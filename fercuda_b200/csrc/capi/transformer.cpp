@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <vector>
 
 namespace fer::capi {
@@ -45,6 +46,16 @@ struct Transformer {
     std::vector<Mark> marks;
     std::vector<cudaEvent_t> spare;
     fer_transformer_profile_t prof{};
+    // CUDA graphs of the forward, one per (tokens, logits, batch, seq): the
+    // second forward with a signature is captured, later ones replay it.
+    struct Graph {
+        const void* tokens;
+        void* logits;
+        int B, Sq;
+        cudaGraphExec_t exec;
+    };
+    std::vector<Graph> graphs;
+    bool graphs_off = false;
 
     cudaEvent_t event() {
         cudaEvent_t e = nullptr;
@@ -66,6 +77,8 @@ struct Transformer {
 
     ~Transformer() {
         if (!S) return;
+        for (auto& g : graphs)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
         release_marks();
         for (cudaEvent_t e : spare) cudaEventDestroy(e);
         for (void* p : {static_cast<void*>(x), static_cast<void*>(a), static_cast<void*>(qkv),
@@ -229,24 +242,61 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
     const double gq = 2.0 * Td * 3 * d * d, go = 2.0 * Td * d * d, g1f = 2.0 * Td * d * F, glm = 2.0 * Td * d * V;
     // causal attention: S(S+1)/2 (query, key) pairs per sequence and head, 2*64 flops each for QK^T and for PV
     const double ga = 4.0 * 64.0 * (static_cast<double>(Sq) * (Sq + 1) / 2.0) * B * c.heads;
-    run(3, 0.0, [&] { return fer_embed_f32(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, Ti, d, V, err, st); });
-    for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
-        const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
-        const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
-        const float* g2 = m->ln + (4 * l + 2) * static_cast<size_t>(d);
-        const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
-        run(2, 0.0, [&] { return fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st); });
-        run(0, gq, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_qkv[l], m->qkv, nullptr, Ti, 3 * d, d, kEpiBF16, err, st); });
-        run(1, ga, [&] { return fer_attn_causal_ex(m->qkv, m->att, B, Sq, d, static_cast<int>(c.heads), 0, err, st); });
-        run(0, go, [&] { return fer_gemm_bf16_tc_ex(m->att, W + m->off_o[l], m->x, m->x, Ti, d, d, kEpiResidF32, err, st); });
-        run(2, 0.0, [&] { return fer_ln_bf16(m->x, g2, b2, m->a, Ti, d, c.eps, st); });
-        run(0, g1f, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_w1[l], m->hid, nullptr, Ti, F, d, kEpiGeluBF16, err, st); });
-        run(0, g1f, [&] { return fer_gemm_bf16_tc_ex(m->hid, W + m->off_w2[l], m->x, m->x, Ti, d, F, kEpiResidF32, err, st); });
+    auto issue = [&]() {
+        run(3, 0.0, [&] { return fer_embed_f32(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, Ti, d, V, err, st); });
+        for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
+            const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
+            const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
+            const float* g2 = m->ln + (4 * l + 2) * static_cast<size_t>(d);
+            const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
+            run(2, 0.0, [&] { return fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st); });
+            run(0, gq, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_qkv[l], m->qkv, nullptr, Ti, 3 * d, d, kEpiBF16, err, st); });
+            run(1, ga, [&] { return fer_attn_causal_ex(m->qkv, m->att, B, Sq, d, static_cast<int>(c.heads), 0, err, st); });
+            run(0, go, [&] { return fer_gemm_bf16_tc_ex(m->att, W + m->off_o[l], m->x, m->x, Ti, d, d, kEpiResidF32, err, st); });
+            run(2, 0.0, [&] { return fer_ln_bf16(m->x, g2, b2, m->a, Ti, d, c.eps, st); });
+            run(0, g1f, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_w1[l], m->hid, nullptr, Ti, F, d, kEpiGeluBF16, err, st); });
+            run(0, g1f, [&] { return fer_gemm_bf16_tc_ex(m->hid, W + m->off_w2[l], m->x, m->x, Ti, d, F, kEpiResidF32, err, st); });
+        }
+        const float* gf = m->ln + (4 * static_cast<size_t>(c.layers)) * d;
+        const float* bf = gf + d;
+        run(2, 0.0, [&] { return fer_ln_bf16(m->x, gf, bf, m->a, Ti, d, c.eps, st); });
+        run(0, glm, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_lm, lb->ptr, nullptr, Ti, V, d, kEpiF32, err, st); });
+    };
+    static int graphs_env = -1;
+    if (graphs_env < 0) {
+        const char* ev = std::getenv("FERCUDA_XFMR_GRAPH");
+        graphs_env = (ev && ev[0] == '0') ? 0 : 1;
     }
-    const float* gf = m->ln + (4 * static_cast<size_t>(c.layers)) * d;
-    const float* bf = gf + d;
-    run(2, 0.0, [&] { return fer_ln_bf16(m->x, gf, bf, m->a, Ti, d, c.eps, st); });
-    run(0, glm, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_lm, lb->ptr, nullptr, Ti, V, d, kEpiF32, err, st); });
+    Transformer::Graph* g = nullptr;
+    if (!m->profiling && graphs_env && !m->graphs_off) {
+        for (auto& x : m->graphs)
+            if (x.tokens == tb->ptr && x.logits == lb->ptr && x.B == B && x.Sq == Sq) g = &x;
+        if (!g && m->graphs.size() < 8) {
+            m->graphs.push_back(Transformer::Graph{tb->ptr, lb->ptr, B, Sq, nullptr});   // first use: eager
+        } else if (g && !g->exec) {
+            // second use: capture the 59 launches once
+            cudaGraph_t graph = nullptr;
+            if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+                issue();
+                const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+                if (e == cudaSuccess && ce == cudaSuccess && graph &&
+                    cudaGraphInstantiate(&g->exec, graph, 0) != cudaSuccess)
+                    g->exec = nullptr;
+                if (graph) cudaGraphDestroy(graph);
+                if (e != cudaSuccess || ce != cudaSuccess || !g->exec) {
+                    cudaGetLastError();
+                    m->graphs_off = true;   // this driver / these kernels: stay eager
+                    g->exec = nullptr;
+                    e = cudaSuccess;
+                }
+            } else {
+                cudaGetLastError();
+                m->graphs_off = true;
+            }
+        }
+    }
+    if (g && g->exec) e = cudaGraphLaunch(g->exec, st);
+    else issue();
     if (e != cudaSuccess) {
         cudaGetLastError();
         return internal("kernel launch failed");

@@ -127,3 +127,36 @@ def test_config_errors(session):
     with pytest.raises(capi.FerError):
         run(session, m, toks, 1000)                              # 128 tokens > max_tokens 64
     m.close()
+
+
+def test_graph_replay_is_bit_identical_to_eager(session):
+    """The forward is issued eagerly the first time a (tokens, logits, batch,
+    seq) signature is seen, captured into a CUDA graph the second time and
+    replayed after that: all three give the same bits, and a replay after the
+    tokens change follows the new tokens."""
+    L, d, h, F, V, B, S = 2, 256, 4, 512, 512, 2, 128
+    m = capi.Transformer(session, L, d, h, F, V, B * S)
+    m.init_weights(7, 0.02)
+    toks = tokens_for(B, S, V, 11)
+    bt = session.alloc(capi.FER_DTYPE_I32, [B, S])
+    bl = session.alloc(capi.FER_DTYPE_F32, [B, S, V])
+    session.upload(bt, toks)
+    outs = []
+    for _ in range(3):
+        session.wait(m.forward(bt, bl))
+        y = np.empty((B, S, V), np.float32)
+        session.download(bl, y)
+        outs.append(y)
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    assert np.array_equal(outs[0].view(np.uint32), outs[2].view(np.uint32))
+    toks2 = tokens_for(B, S, V, 12)
+    session.upload(bt, toks2)
+    session.wait(m.forward(bt, bl))
+    y2 = np.empty((B, S, V), np.float32)
+    session.download(bl, y2)
+    ref2 = run(session, m, toks2, V).cpu().numpy()   # other buffers: an eager forward
+    assert np.array_equal(y2.view(np.uint32), ref2.view(np.uint32))
+    assert session.device_errors() == 0
+    session.free(bt)
+    session.free(bl)
+    m.close()
