@@ -215,8 +215,10 @@ class Chain(Rows):
         self.s, self.capi = s, capi
         c = synth.FUSED_ELEMENTWISE
         self.n, self.a, self.b = n, c["a"], c["b"]
-        self.x = synth.fused_elementwise_input(n)
-        self.nbuf = max(3, (384 << 20) // (8 * n))
+        # sizes above 2^22 repeat the seeded 2^22 prefix (bandwidth sweeps)
+        self.x = synth.fused_elementwise_input(n) if n <= (1 << 22) else np.resize(
+            synth.fused_elementwise_input(1 << 22), n)
+        self.nbuf = max(2, min(48, (384 << 20) // (8 * n)))
         self.pairs = []
         for _ in range(self.nbuf):
             bx, by = s.alloc(capi.FER_DTYPE_F32, [n]), s.alloc(capi.FER_DTYPE_F32, [n])
@@ -237,9 +239,12 @@ class Chain(Rows):
         if st.code:
             raise RuntimeError(st.message)
 
+    def config(self, world):
+        return self.describe(world, self.n)
+
     @staticmethod
     def describe(world, n=1 << 20):
-        nbuf = max(3, (384 << 20) // (8 * n))
+        nbuf = max(2, min(48, (384 << 20) // (8 * n)))
         return {"workload": f"fused_elementwise_relu_affine_mul_sigmoid_{n}_f32", "n": n, "a": 1.5,
                 "b": -0.25, "input": "U(-4,4) seed 0",
                 "l2": f"rotating {nbuf} input/output pairs ({nbuf * 8 * n >> 20} MiB > 126 MB L2)",
@@ -680,6 +685,8 @@ def main():
     ap.add_argument("--workload", default="transformer", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-subresults", action="store_true")
+    ap.add_argument("--elements", type=int, default=None,
+                    help="fused_elementwise only: stream length (default 2^20, the configured workload)")
     ap.add_argument("--global-batch", type=int, default=None,
                     help="transformer only: a smaller global batch (profiling case); default 64")
     args = ap.parse_args()
@@ -703,6 +710,11 @@ def main():
 
     cls = WORKLOADS[args.workload]
     pool = 12 << 30 if cls is Transformer else 4 << 30
+    if cls is Chain and args.elements:
+        # the session pool is split into mutable / immutable halves; the
+        # rotating x / y buffers all come from the mutable half
+        nbuf = max(2, min(48, (384 << 20) // (8 * args.elements)))
+        pool = max(pool, 2 * (2 * nbuf * 4 * args.elements) + (1 << 30))
     s = capi.Session(local, pool_bytes=pool)
     stream = torch.cuda.ExternalStream(s.stream())
 
@@ -725,7 +737,7 @@ def main():
 
     wl = cls(s, capi, synth, rank=rank, world=world, dist=dist, torch=torch, batch=args.global_batch) \
         if cls is Transformer \
-        else cls(s, capi, synth)
+        else (cls(s, capi, synth, n=args.elements) if cls is Chain and args.elements else cls(s, capi, synth))
 
     clocks = ClockSampler(local)
     clocks.start()
