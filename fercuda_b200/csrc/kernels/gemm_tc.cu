@@ -37,6 +37,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 
 namespace {
@@ -390,7 +391,7 @@ constexpr int A2_BYTES = 128 * BK * 2;            // 16 KiB: this CTA's 128 rows
 constexpr int B2_BYTES = BK * 128 * 2;            // 16 KiB: this CTA's 128 columns (two 64-column panels)
 constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + EPI_WARPS * STAGING_BYTES + 1024;
-constexpr int GROUP_M2 = 8;                       // 256-row blocks per raster group
+constexpr int GROUP_M2 = 8;                       // default 256-row blocks per raster group
 // kind::f16, f32 accumulator, bf16 A/B, A K-major, B N-major, N = 256, M = 256.
 constexpr uint32_t kIdesc2 = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (static_cast<uint32_t>(256 >> 3) << 17) |
                              (static_cast<uint32_t>(256 >> 4) << 24);
@@ -455,11 +456,11 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
-__device__ __forceinline__ void tile_coords2(int t, int num_m2, int num_n, int* mb, int* nb) {
-    const int per_group = GROUP_M2 * num_n;
+__device__ __forceinline__ void tile_coords2(int t, int num_m2, int num_n, int group_m, int* mb, int* nb) {
+    const int per_group = group_m * num_n;
     const int g = t / per_group;
-    const int first_m = g * GROUP_M2;
-    const int gm = (num_m2 - first_m) < GROUP_M2 ? (num_m2 - first_m) : GROUP_M2;
+    const int first_m = g * group_m;
+    const int gm = (num_m2 - first_m) < group_m ? (num_m2 - first_m) : group_m;
     const int r = t - g * per_group;
     *mb = first_m + r % gm;
     *nb = r / gm;
@@ -467,7 +468,8 @@ __device__ __forceinline__ void tile_coords2(int t, int num_m2, int num_n, int* 
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, uint32_t* err) {
+                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, int group_m,
+                         uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars2 bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -510,7 +512,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int it = 0;
         for (int t = cid; t < num_tiles && !warp_flag(abort_flag); t += ncl) {
             int mb, nb;
-            tile_coords2(t, num_m2, num_n, &mb, &nb);
+            tile_coords2(t, num_m2, num_n, group_m, &mb, &nb);
             const int row = mb * 256 + static_cast<int>(rank) * 128;
             const int col = nb * BN + static_cast<int>(rank) * 128;
             for (int kt = 0; kt < num_k; ++kt, ++it) {
@@ -596,7 +598,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             int mb, nb;
-            tile_coords2(t, num_m2, num_n, &mb, &nb);
+            tile_coords2(t, num_m2, num_n, group_m, &mb, &nb);
             const int row0 = mb * 256 + static_cast<int>(rank) * 128 + q * 32;
             const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(buf * BN + half * (BN / 2));
@@ -672,6 +674,29 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// Tuning knobs read once per process: FERCUDA_GEMM_GROUP (256-row blocks
+// per raster group of the 2-CTA kernel) and FERCUDA_GEMM_L2_PROMOTION
+// (0 none, 1 64 B, 2 128 B, 3 256 B for the TMA loads).
+int gemm_group_m() {
+    static int g = 0;
+    if (!g) {
+        const char* e = std::getenv("FERCUDA_GEMM_GROUP");
+        g = e ? std::atoi(e) : GROUP_M2;
+        if (g < 1) g = GROUP_M2;
+    }
+    return g;
+}
+
+int l2_promotion() {
+    static int p = -1;
+    if (p < 0) {
+        const char* e = std::getenv("FERCUDA_GEMM_L2_PROMOTION");
+        p = e ? std::atoi(e) : static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+        if (p < 0 || p > 3) p = static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    }
+    return p;
+}
+
 // 2-D tensor map over a row-major [rows, cols] matrix of 2- or 4-byte
 // elements, box [box_rows, 128 bytes], 128-byte swizzle.
 bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
@@ -684,7 +709,7 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
     const cuuint32_t box[2] = {128u / esize, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_SWIZZLE_128B, static_cast<CUtensorMapL2promotion>(l2_promotion()),
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -757,7 +782,8 @@ extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c
         if (clusters > 0) {
             const int tiles2 = ((M + 255) / 256) * ((N + BN - 1) / BN);
             const int ncl = tiles2 < clusters ? tiles2 : clusters;
-            gemm_bf16_tc2_kernel<<<2 * ncl, kThreads, SMEM2_BYTES, stream>>>(ma, mb, mc, M, N, K, epi, err);
+            gemm_bf16_tc2_kernel<<<2 * ncl, kThreads, SMEM2_BYTES, stream>>>(ma, mb, mc, M, N, K, epi,
+                                                                               gemm_group_m(), err);
             return cudaGetLastError();
         }
     }
