@@ -9,7 +9,9 @@
 //   warp 0      TMA: Q once, K_j into a 2-deep ring, V_j into one buffer,
 //               all 128-byte swizzled [128 rows x 64 bf16] boxes
 //   warp 1      tcgen05.mma from one thread: S = Q K_j^T (M128 N128, f32 in
-//               tensor memory), then O_j = P_j V_j (M128 N64, K = 128 keys)
+//               tensor memory), issued for block j+1 as soon as the softmax
+//               threads have read block j's scores, then O += P_j V_j (M128
+//               N64, K = 128 keys) once P_j is written
 //   warps 2..5  one query row per thread: scores from tensor memory
 //               (tcgen05.ld), causal mask on the diagonal block, running max
 //               in the log2 domain, p = 2^(s*scale - m) (ex2.approx), row sum
@@ -237,14 +239,13 @@ __global__ void __launch_bounds__(kThreads, 2)
             __syncwarp();
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer
-        bool ok = warp_wait(&bars.q_full, 0);
-        for (int j = 0; j < n_k && ok && !warp_flag(abort_flag); ++j) {
+        // ---------------- MMA issuer: S_{j+1} goes in as soon as the softmax
+        // threads have read S_j, so it runs under their exponentials; P_j V_j
+        // follows once P_j is written.
+        auto issue_s = [&](int j) -> bool {
             const int st = j & 1;
-            const uint32_t use = static_cast<uint32_t>(j >> 1);
-            const uint32_t ph = static_cast<uint32_t>(j) & 1u, prev = ph ^ 1u;
-            ok = warp_wait(&bars.k_full[st], use & 1u) && (j == 0 || warp_wait(&bars.s_free, prev));
-            if (!ok) break;
+            if (!warp_wait(&bars.k_full[st], static_cast<uint32_t>(j >> 1) & 1u)) return false;
+            if (j > 0 && !warp_wait(&bars.s_free, static_cast<uint32_t>(j - 1) & 1u)) return false;
             fence_after();
             if (lane == 0) {
                 const uint32_t q = sbase + OFF_Q, k = sbase + OFF_K + st * TILE_BYTES;
@@ -255,6 +256,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                 commit(&bars.s_full);
             }
             __syncwarp();
+            return true;
+        };
+        bool ok = warp_wait(&bars.q_full, 0) && issue_s(0);
+        for (int j = 0; j < n_k && ok && !warp_flag(abort_flag); ++j) {
+            const uint32_t ph = static_cast<uint32_t>(j) & 1u;
+            if (j + 1 < n_k && !(ok = issue_s(j + 1))) break;
             ok = warp_wait(&bars.p_full, ph) && warp_wait(&bars.v_full, ph);
             if (!ok) break;
             fence_after();
@@ -286,16 +293,13 @@ __global__ void __launch_bounds__(kThreads, 2)
                 ok = false;
                 break;
             }
-            // S_j's commit follows P_{j-1} V_{j-1} in issue order, so this
-            // wait returns at once; after it P's buffer and O are ours.
-            if (j > 0 && !warp_wait(&bars.o_full, ph ^ 1u)) {
-                ok = false;
-                break;
-            }
             fence_after();
             float sv[128];
             tmem_ld64(trow, sv);
             tmem_ld64(trow + 64, sv + 64);
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.s_free);   // S_{j+1} may overwrite S now
             if (j == qt) {
 #pragma unroll
                 for (int e = 0; e < 128; ++e)
@@ -310,6 +314,13 @@ __global__ void __launch_bounds__(kThreads, 2)
                                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             const float m_new = fmaxf(m, smax * scale_log2);
             const float alpha = ex2(m - m_new);
+            // P_{j-1} V_{j-1} done: P's buffer is free and O holds every
+            // earlier block
+            if (j > 0 && !warp_wait(&bars.o_full, ph ^ 1u)) {
+                ok = false;
+                break;
+            }
+            fence_after();
             // p = 2^(s*scale - m_new), row sum, P (bf16) into shared memory
             float sm[8];
 #pragma unroll
@@ -351,10 +362,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             fence_proxy_async_smem();   // P is read by the tensor core (async proxy)
             fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&bars.s_free);
-                mbar_arrive(&bars.p_full);
-            }
+            if (lane == 0) mbar_arrive(&bars.p_full);
         }
         if (ok && !warp_wait(&bars.o_full, static_cast<uint32_t>(n_k - 1) & 1u)) ok = false;
         if (!ok) {
