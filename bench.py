@@ -624,11 +624,41 @@ def subresults(s, capi, synth, torch, stream):
             for bx, by in wl.pairs:
                 s.free(bx)
                 s.free(by)
+    out["alloc_hook"] = hook_alloc_pairs(capi)
     tl = Tlsf(s, capi, synth).run(ops=100_000)
     out["tlsf"] = {"metric": Tlsf.metric, "value": tl["tlsf"]["alloc_p50_ns"], "unit": "ns", "results": tl,
                    "sample": "first 100k ops of the 1M-op trace (full trace: --workload tlsf)",
                    "reference_tlsf_host": Tlsf.cpu_reference(ops=100_000)}
     return out
+
+
+def hook_alloc_pairs(capi, iters=50_000, cuda_iters=5_000, warmup=1_000, nbytes=65536):
+    """The reference's allocator claim ("TLSF ~100-200x faster than cudaMalloc
+    for alloc+free"; workload tests/bench/bench_alloc_vs_cudamalloc.cu:21-25,
+    89-114): fer_alloc_bench times 64 KiB cudaMalloc + cudaFree pairs natively
+    and under LD_PRELOAD=libptx_hook.so (pairs served by the TLSF pool), each
+    in its own process. A native pair costs hundreds of microseconds on a
+    B200, so the native leg runs `cuda_iters` pairs (seconds) instead of the
+    claim's 50,000 (minutes); the hooked leg runs all `iters`."""
+    import subprocess
+
+    res = {}
+    for name, preload, n in (("cudaMalloc", False, cuda_iters), ("tlsf_hook", True, iters)):
+        args = [str(capi.LIBDIR / "fer_alloc_bench"), "--iters", str(n), "--warmup", str(warmup if preload else 100),
+                "--bytes", str(nbytes)]
+        env = {k: v for k, v in os.environ.items() if not k.startswith("PTX_") and k != "LD_PRELOAD"}
+        if preload:
+            env.update(LD_PRELOAD=str(capi.LIBDIR / "libptx_hook.so"), PTX_POOL_SIZE=str(256 << 20))
+        r = subprocess.run(args, env=env, capture_output=True, text=True, timeout=600)
+        kv = dict(line.split("=", 1) for line in r.stdout.splitlines() if "=" in line)
+        res[name] = {"rc": r.returncode, **{k: (v if k == "mode" else float(v)) for k, v in kv.items()}}
+    ok = all(v["rc"] == 0 for v in res.values())
+    speedup = (res["cudaMalloc"]["ns_per_alloc_free"] / res["tlsf_hook"]["ns_per_alloc_free"]) if ok else None
+    return {"metric": "64 KiB cudaMalloc+cudaFree pair, ns", "value": res["tlsf_hook"].get("ns_per_alloc_free"),
+            "unit": "ns", "speedup_vs_cudamalloc": round(speedup, 1) if speedup else None,
+            "reference_published": "TLSF ~100-200x faster than cudaMalloc for alloc+free (README.md:311)",
+            "sample": f"hook: {iters} pairs after {warmup} warm-up; cudaMalloc: {cuda_iters} pairs after 100; "
+                      "host clock, each leg in its own process", "results": res}
 
 
 def run_reference(args, rank):

@@ -17,6 +17,7 @@ HEADERS = {
                            "include/fercuda/jit/intent/intent.h", "include/fercuda/b200/ext.h"],
     "libptx_core.so": ["include/ptx/memory/ptx_tlsf_allocator.h", "include/ptx/gpu/gpu_hot_runtime.h"],
     "libptx_kernels.so": ["include/ptx/gpu/tensor_ops.h", "include/fercuda/b200/native.h"],
+    "libptx_hook.so": ["include/ptx/ptx_hook.h"],
 }
 REFERENCE = Path("/root/reference")
 
@@ -38,7 +39,7 @@ def test_library_exports_every_declared_symbol(lib):
                          check=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
     names = [n for h in HEADERS[lib] for n in declared(ROOT / h)]
-    assert len(names) > 5
+    assert len(names) >= 4
     missing = sorted(set(names) - exported)
     assert not missing, missing
 
