@@ -72,41 +72,23 @@ fer_status_t fer_submit_layer_norm(fer_session_t* session, const fer_layer_norm_
     if (!compute_dtype(x->desc.dtype) || !compute_dtype(o->desc.dtype))
         return invalid("layer_norm requires supported buffers (f32/f16/bf16/i8/u8)");
     if (x->desc.dtype != o->desc.dtype) return invalid("layer_norm requires matching dtypes for x/out");
-    if (x->desc.rank != 1 || o->desc.rank != 1) return invalid("layer_norm requires rank-1 buffers");
-    if (o->numel != x->numel) return invalid("layer_norm shape mismatch");
-    const int n = static_cast<int>(x->numel);
-    std::vector<Temp> temps;
-    fer_status_t st;
-    if (x->desc.dtype == FER_DTYPE_F32) {
-        st = launched(fer_rows_f32(static_cast<const float*>(x->ptr), static_cast<float*>(o->ptr), nullptr, nullptr, 1,
-                                   n, req->eps, FER_ROWS_LAYER_NORM, S.dev_err, S.stream));
-    } else {
-        // Same staging as the reference (exec_planner.cu:304-387): cast to an
-        // f32 temporary, normalise, cast back.
-        Temp tx{}, ty{};
-        st = S.alloc_temp(static_cast<size_t>(n) * 4, req->memory_regime, &tx);
-        if (st.code != FER_STATUS_OK) return st;
-        temps.push_back(tx);
-        st = S.alloc_temp(static_cast<size_t>(n) * 4, req->memory_regime, &ty);
-        if (st.code != FER_STATUS_OK) {
-            S.free_bytes(tx.ptr, tx.regime, tx.tier, tx.bytes);
-            return st;
-        }
-        temps.push_back(ty);
-        cudaError_t e = fer_cast_to_f32(x->ptr, static_cast<float*>(tx.ptr), n, x->desc.dtype, S.stream);
-        if (e == cudaSuccess)
-            e = fer_rows_f32(static_cast<const float*>(tx.ptr), static_cast<float*>(ty.ptr), nullptr, nullptr, 1, n,
-                             req->eps, FER_ROWS_LAYER_NORM, S.dev_err, S.stream);
-        if (e == cudaSuccess) e = fer_cast_from_f32(static_cast<const float*>(ty.ptr), o->ptr, n, o->desc.dtype, S.stream);
-        st = launched(e);
-        if (st.code != FER_STATUS_OK) {
-            for (const Temp& t : temps) S.free_bytes(t.ptr, t.regime, t.tier, t.bytes);
-            return st;
-        }
-    }
+    // Rank 1: one row, as in the reference. Rank 2 [rows, cols]: every row
+    // normalised (additive; the reference accepts rank 1 only).
+    if (x->desc.rank < 1 || x->desc.rank > 2 || o->desc.rank != x->desc.rank)
+        return invalid("layer_norm requires rank-1 buffers");
+    if (o->numel != x->numel || (x->desc.rank == 2 && (o->desc.dims[0] != x->desc.dims[0] ||
+                                                       o->desc.dims[1] != x->desc.dims[1])))
+        return invalid("layer_norm shape mismatch");
+    const int rows = x->desc.rank == 2 ? static_cast<int>(x->desc.dims[0]) : 1;
+    const int cols = static_cast<int>(x->desc.dims[x->desc.rank - 1]);
+    // Every dtype in one launch, no f32 temporaries: the kernel widens on
+    // load and rounds on store exactly as the reference's cast staging does
+    // (exec_planner.cu:304-387).
+    fer_status_t st = launched(fer_layer_norm_typed(x->ptr, o->ptr, rows, cols, req->eps, x->desc.dtype, S.dev_err,
+                                                    S.stream));
     if (st.code != FER_STATUS_OK) return st;
     uint64_t job = 0;
-    st = S.make_job(std::move(temps), &job);
+    st = S.make_job({}, &job);
     if (st.code == FER_STATUS_OK && out_job_id) *out_job_id = job;
     return st;
 }

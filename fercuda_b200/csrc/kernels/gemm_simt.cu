@@ -11,51 +11,15 @@
 //   - each thread keeps an 8x8 block of accumulators in registers over a
 //     128x128 output tile (the reference: one output per thread, 16x16 tiles).
 // The K order per output is untouched: it is the chain that fixes the bits.
-#include <cuda_bf16.h>
-#include <cuda_fp16.h>
+#include "elem.cuh"
+
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 namespace {
 
-// Buffer dtype codes of the C ABI (fer_buffer_dtype_t).
-enum : uint32_t { kF32 = 0, kF16 = 1, kBF16 = 2, kI8 = 3, kU8 = 4 };
-
-template <uint32_t DT> struct Elem;
-template <> struct Elem<kF32> {
-    using T = float;
-    __device__ static float load(const T* p, size_t i) { return p[i]; }
-    __device__ static void store(T* p, size_t i, float v) { p[i] = v; }
-};
-template <> struct Elem<kF16> {
-    using T = __half;
-    __device__ static float load(const T* p, size_t i) { return __half2float(p[i]); }
-    __device__ static void store(T* p, size_t i, float v) { p[i] = __float2half_rn(v); }
-};
-template <> struct Elem<kBF16> {
-    using T = __nv_bfloat16;
-    __device__ static float load(const T* p, size_t i) { return __bfloat162float(p[i]); }
-    __device__ static void store(T* p, size_t i, float v) { p[i] = __float2bfloat16(v); }
-};
-template <> struct Elem<kI8> {
-    using T = int8_t;
-    __device__ static float load(const T* p, size_t i) { return static_cast<float>(p[i]); }
-    __device__ static void store(T* p, size_t i, float v) {
-        if (v > 127.0f) v = 127.0f;
-        if (v < -128.0f) v = -128.0f;
-        p[i] = static_cast<int8_t>(nearbyintf(v));
-    }
-};
-template <> struct Elem<kU8> {
-    using T = uint8_t;
-    __device__ static float load(const T* p, size_t i) { return static_cast<float>(p[i]); }
-    __device__ static void store(T* p, size_t i, float v) {
-        if (v > 255.0f) v = 255.0f;
-        if (v < 0.0f) v = 0.0f;
-        p[i] = static_cast<uint8_t>(nearbyintf(v));
-    }
-};
+using namespace fer::dev;
 
 constexpr int BM = 128, BN = 128, BK = 16, TM = 8, TN = 8;
 constexpr int kThreads = (BM / TM) * (BN / TN);  // 256

@@ -25,6 +25,7 @@
 // Shapes the bulk-copy path cannot take (cols < 256, cols % 4 != 0, a
 // misaligned base, cols > 16384) run a multi-pass kernel with the same
 // arithmetic.
+#include "elem.cuh"
 #include "sm100_util.cuh"
 
 #include <cuda_runtime.h>
@@ -410,6 +411,53 @@ __global__ void __launch_bounds__(kThreads) rows_generic_kernel(RowsArgs a) {
     }
 }
 
+// Layer norm of f16 / bf16 / i8 / u8 rows, one CTA per row: each value is
+// widened to f32 on load, normalised with the arithmetic of the layer-norm
+// pass above (the reference's k_layer_norm_f32 order), and rounded back with
+// the reference's cast. That is what the reference computes through f32
+// temporaries (exec_planner.cu:304-387: cast, normalise, cast back), bit for
+// bit, in one launch and without the temporaries. In place (x == y) is
+// allowed: a row is written only after its last read.
+template <uint32_t DT>
+__global__ void __launch_bounds__(kThreads) ln_typed_kernel(const typename Elem<DT>::T* x, typename Elem<DT>::T* y,
+                                                            int rows, int cols, float eps) {
+    __shared__ float sdata[kThreads];
+    const int t = threadIdx.x;
+    const int T = cols < kThreads ? cols : kThreads;
+    const float n = static_cast<float>(cols);
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const size_t base = static_cast<size_t>(r) * cols;
+        float s = 0.0f;
+        if (t < T)
+            for (int c = t; c < cols; c += T) s += Elem<DT>::load(x, base + c);
+        sdata[t] = s;
+        __syncthreads();
+        for (int h = T / 2; h > 0; h >>= 1) {
+            if (t < h) sdata[t] += sdata[t + h];
+            __syncthreads();
+        }
+        const float mean = sdata[0] / n;
+        __syncthreads();
+        float q = 0.0f;
+        if (t < T)
+            for (int c = t; c < cols; c += T) {
+                const float d = Elem<DT>::load(x, base + c) - mean;
+                q += d * d;
+            }
+        sdata[t] = q;
+        __syncthreads();
+        for (int h = T / 2; h > 0; h >>= 1) {
+            if (t < h) sdata[t] += sdata[t + h];
+            __syncthreads();
+        }
+        const float inv_std = rsqrtf(sdata[0] / n + eps);
+        __syncthreads();
+        if (t < T)
+            for (int c = t; c < cols; c += T)
+                Elem<DT>::store(y, base + c, (Elem<DT>::load(x, base + c) - mean) * inv_std);
+    }
+}
+
 int g_num_sms = 0;
 
 int num_sms() {
@@ -508,6 +556,37 @@ extern "C" cudaError_t fer_rows_f32(const float* x, float* y, const float* gamma
     }
     int grid = rows < num_sms() * 8 ? rows : num_sms() * 8;
     rows_generic_kernel<<<grid, kThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+// Layer norm of each row of a [rows, cols] buffer of dtype `dtype`
+// (fer_buffer_dtype_t: 0 f32, 1 f16, 2 bf16, 3 i8, 4 u8), no affine.
+extern "C" cudaError_t fer_layer_norm_typed(const void* x, void* y, int rows, int cols, float eps, uint32_t dtype,
+                                            uint32_t* err, cudaStream_t stream) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    if (dtype == kF32)
+        return fer_rows_f32(static_cast<const float*>(x), static_cast<float*>(y), nullptr, nullptr, rows, cols, eps,
+                            kLayerNorm, err, stream);
+    const int grid = rows < num_sms() * 8 ? rows : num_sms() * 8;
+    switch (dtype) {
+        case kF16:
+            ln_typed_kernel<kF16><<<grid, kThreads, 0, stream>>>(static_cast<const __half*>(x),
+                                                                 static_cast<__half*>(y), rows, cols, eps);
+            break;
+        case kBF16:
+            ln_typed_kernel<kBF16><<<grid, kThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
+                                                                  static_cast<__nv_bfloat16*>(y), rows, cols, eps);
+            break;
+        case kI8:
+            ln_typed_kernel<kI8><<<grid, kThreads, 0, stream>>>(static_cast<const int8_t*>(x),
+                                                                static_cast<int8_t*>(y), rows, cols, eps);
+            break;
+        case kU8:
+            ln_typed_kernel<kU8><<<grid, kThreads, 0, stream>>>(static_cast<const uint8_t*>(x),
+                                                                static_cast<uint8_t*>(y), rows, cols, eps);
+            break;
+        default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

@@ -64,6 +64,14 @@ cudaError_t fer_rows_f32(const float* x, float* y, const float* gamma, const flo
                          float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
                               float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
+/* Layer norm of every row of x [rows, cols] (no affine) for any buffer dtype
+ * (fer_buffer_dtype_t): computed in f32 in the reference order, each value
+ * widened on load and rounded back on store as the reference's cast staging
+ * does (src/runtime/exec_planner.cu:304-387), so the bits equal cast ->
+ * fer_rows_f32 -> cast; one launch, no temporaries; x == y allowed. f32 runs
+ * fer_rows_f32. */
+cudaError_t fer_layer_norm_typed(const void* x, void* y, int rows, int cols, float eps, uint32_t dtype,
+                                 uint32_t* err, cudaStream_t stream);
 
 /* ---- intents -------------------------------------------------------------------
  * Deterministic sum / max of n floats into out[0] (sum adds to out[0], as the

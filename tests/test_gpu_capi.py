@@ -350,3 +350,76 @@ def test_pool_stats_and_raw(session):
     capi.check("free", session.call("fer_pool_free_raw", p))
     st = session.call("fer_pool_free_raw", p)
     assert st.code == capi.FER_STATUS_NOT_FOUND
+
+
+def _ln_input(dt, n, seed):
+    """Host data of dtype `dt` and its numpy container for download."""
+    if dt == capi.FER_DTYPE_F32:
+        return synth.normal_f32(seed, n) * 3 + 1, np.float32
+    if dt == capi.FER_DTYPE_F16:
+        return f16(synth.normal_f32(seed, n) * 3 + 1), np.uint16
+    if dt == capi.FER_DTYPE_BF16:
+        return synth.f32_to_bf16_bits(synth.normal_f32(seed, n) * 3 + 1), np.uint16
+    u = synth.uniform01(seed, n)
+    if dt == capi.FER_DTYPE_I8:
+        return (u * 255 - 128).astype(np.int8), np.int8
+    return (u * 255).astype(np.uint8), np.uint8
+
+
+@pytest.mark.parametrize("dt", [capi.FER_DTYPE_F32, capi.FER_DTYPE_F16, capi.FER_DTYPE_BF16, capi.FER_DTYPE_I8,
+                                capi.FER_DTYPE_U8])
+@pytest.mark.parametrize("shape", [[4], [1000], [4096], [37, 300], [3, 100], [5, 1], [2, 8192]])
+def test_layer_norm_any_dtype_equals_cast_staging(session, dt, shape):
+    """fer_submit_layer_norm on a non-f32 buffer runs one kernel with no f32
+    temporaries; its bits equal the reference's staging (cast to f32,
+    k_layer_norm_f32 order, cast back; exec_planner.cu:304-387), run here
+    explicitly with fer_cast_to_f32 -> fer_rows_f32 -> fer_cast_from_f32.
+    Rank 2 normalises every row (row-batched)."""
+    k = capi.kernels()
+    n = int(np.prod(shape))
+    rows, cols = (shape[0], shape[1]) if len(shape) == 2 else (1, shape[0])
+    host, npdt = _ln_input(dt, n, 90 + n)
+    bx, by = session.alloc(dt, shape), session.alloc(dt, shape)
+    tx, ty = session.alloc(capi.FER_DTYPE_F32, [n]), session.alloc(capi.FER_DTYPE_F32, [n])
+    bs = session.alloc(dt, shape)
+    session.upload(bx, host)
+    job = C.c_uint64()
+    req = capi.fer_layer_norm_request_t(bx, by, 1e-5, capi.FER_MEMORY_AUTO)
+    capi.check("ln", session.call("fer_submit_layer_norm", C.byref(req), C.byref(job)))
+    session.wait(job.value)
+    P, st = C.c_void_p, session.stream()
+    k.fer_cast_to_f32.argtypes = [P, P, C.c_size_t, C.c_uint32, P]
+    k.fer_cast_from_f32.argtypes = [P, P, C.c_size_t, C.c_uint32, P]
+    k.fer_rows_f32.argtypes = [P, P, P, P, C.c_int, C.c_int, C.c_float, C.c_uint32, P, P]
+    for f in (k.fer_cast_to_f32, k.fer_cast_from_f32, k.fer_rows_f32):
+        f.restype = C.c_int
+    assert k.fer_cast_to_f32(session.ptr_of(bx), session.ptr_of(tx), n, dt, st) == 0
+    assert k.fer_rows_f32(session.ptr_of(tx), session.ptr_of(ty), None, None, rows, cols, 1e-5, 2, None, st) == 0
+    assert k.fer_cast_from_f32(session.ptr_of(ty), session.ptr_of(bs), n, dt, st) == 0
+    got, staged = np.empty(n, npdt), np.empty(n, npdt)
+    session.download(by, got)
+    session.download(bs, staged)
+    assert np.array_equal(got.view(np.uint8), staged.view(np.uint8))
+    if dt in (capi.FER_DTYPE_F16, capi.FER_DTYPE_BF16) and cols > 1 and (cols >= 256 or cols & (cols - 1) == 0):
+        # and the values are a layer norm of each row (bf16 / f16 output
+        # rounding); rows shorter than 256 and not a power of two follow the
+        # reference's halving tree, which drops partials (ops_bridge.cu:41-45)
+        x = (host.view(np.float16).astype(np.float32) if dt == capi.FER_DTYPE_F16 else synth.bf16_bits_to_f32(host))
+        x = x.reshape(rows, cols).astype(np.float64)
+        ref = (x - x.mean(1, keepdims=True)) / np.sqrt(x.var(1, keepdims=True) + 1e-5)
+        y = got.view(np.float16).astype(np.float32) if dt == capi.FER_DTYPE_F16 else synth.bf16_bits_to_f32(got)
+        assert np.abs(y.reshape(rows, cols) - ref).max() <= (2e-2 if dt == capi.FER_DTYPE_BF16 else 4e-3)
+    for b in (bx, by, tx, ty, bs):
+        session.free(b)
+
+
+def test_layer_norm_rank_checks(session):
+    x2 = session.alloc(capi.FER_DTYPE_F16, [4, 8])
+    y1 = session.alloc(capi.FER_DTYPE_F16, [32])
+    y2 = session.alloc(capi.FER_DTYPE_F16, [8, 4])
+    x3 = session.alloc(capi.FER_DTYPE_F16, [2, 2, 8])
+    job = C.c_uint64()
+    for x, y, msg in ((x2, y1, "rank-1"), (x2, y2, "shape mismatch"), (x3, x3, "rank-1")):
+        req = capi.fer_layer_norm_request_t(x, y, 1e-5, capi.FER_MEMORY_AUTO)
+        st = session.call("fer_submit_layer_norm", C.byref(req), C.byref(job))
+        assert st.code == capi.FER_STATUS_INVALID_ARGUMENT and msg in st.message.decode(), st.message
