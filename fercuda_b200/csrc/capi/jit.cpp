@@ -332,6 +332,8 @@ fer_status_t chain_source(const fer_chain_op_t* ops, uint32_t n, uint32_t n_inpu
         << "extern \"C\" __global__ void __launch_bounds__(256) fer_chain_v4(\n"
            "    const float4* __restrict__ a0, const float4* __restrict__ a1, const float4* __restrict__ a2,\n"
            "    const float4* __restrict__ a3, float4* __restrict__ out, unsigned long long n4, FerChainParams p) {\n"
+           "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
+           "  asm volatile(\"griddepcontrol.launch_dependents;\");\n"
            "  const unsigned long long stride = (unsigned long long)gridDim.x * 256ull;\n"
            "  unsigned long long i = (unsigned long long)blockIdx.x * 256ull + threadIdx.x;\n"
            "  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);\n"
@@ -366,6 +368,8 @@ fer_status_t chain_source(const fer_chain_op_t* ops, uint32_t n, uint32_t n_inpu
            "extern \"C\" __global__ void __launch_bounds__(256) fer_chain_s1(\n"
            "    const float* a0, const float* a1, const float* a2, const float* a3, float* out,\n"
            "    unsigned long long lo, unsigned long long n, FerChainParams p) {\n"
+           "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
+           "  asm volatile(\"griddepcontrol.launch_dependents;\");\n"
            "  const unsigned long long stride = (unsigned long long)gridDim.x * 256ull;\n"
            "  for (unsigned long long i = lo + (unsigned long long)blockIdx.x * 256ull + threadIdx.x; i < n; i += stride)\n"
            "    out[i] = fer_chain_eval(a0 ? a0[i] : 0.f, a1 ? a1[i] : 0.f, a2 ? a2[i] : 0.f, a3 ? a3[i] : 0.f, p);\n"
@@ -710,6 +714,29 @@ int sm_count() {
     return n;
 }
 
+// Programmatic dependent launch: the kernel may be scheduled while the
+// previous kernel on the stream drains; the chain kernels begin with
+// griddepcontrol.wait, which holds them until that kernel has completed and
+// its writes are visible, so only the launch latency overlaps.
+cudaError_t launch_pdl(const void* fn, unsigned grid, void** args, cudaStream_t stream) {
+    static const bool pdl = [] {
+        const char* e = std::getenv("FERCUDA_CHAIN_PDL");   // 0: plain launches
+        return !(e && e[0] == '0');
+    }();
+    if (!pdl) return cudaLaunchKernel(fn, dim3(grid), dim3(256), args, 0, stream);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 // Launches a compiled chain over n elements of device streams.
 fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op_t* ops, uint32_t n_ops,
                           const float* const* in, uint32_t n_inputs, float* out, uint64_t n) {
@@ -731,8 +758,8 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
         uint64_t g = (n4 + 255) / 256;
         if (g > cap) g = cap;
         void* args[] = {&a[0], &a[1], &a[2], &a[3], &out, &n4, &p};
-        if (cudaLaunchKernel(reinterpret_cast<const void*>(ck.v4), dim3(static_cast<unsigned>(g)), dim3(256), args, 0,
-                             S.stream) != cudaSuccess) {
+        if (launch_pdl(reinterpret_cast<const void*>(ck.v4), static_cast<unsigned>(g), args, S.stream) !=
+            cudaSuccess) {
             cudaGetLastError();
             return internal("kernel launch failed");
         }
@@ -743,8 +770,8 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
         uint64_t g = (n - done + 255) / 256;
         if (g > cap) g = cap;
         void* args[] = {&a[0], &a[1], &a[2], &a[3], &out, &lo, &hi, &p};
-        if (cudaLaunchKernel(reinterpret_cast<const void*>(ck.s1), dim3(static_cast<unsigned>(g)), dim3(256), args, 0,
-                             S.stream) != cudaSuccess) {
+        if (launch_pdl(reinterpret_cast<const void*>(ck.s1), static_cast<unsigned>(g), args, S.stream) !=
+            cudaSuccess) {
             cudaGetLastError();
             return internal("kernel launch failed");
         }

@@ -154,8 +154,27 @@ fer_status_t Session::add_buffer(const fer_buffer_desc_t& d, void* ptr, uint32_t
     return ok();
 }
 
+// A caller that never polls its jobs would otherwise cost one
+// cudaEventCreate per submission: once 64 jobs are outstanding, the oldest
+// (by then normally complete) is finalized and its event reused.
+void Session::reclaim_oldest() {
+    while (!pending.empty()) {
+        auto it = jobs.find(pending.front());
+        if (it == jobs.end() || it->second.finalized) {
+            pending.pop_front();
+            continue;
+        }
+        if (cudaEventQuery(it->second.ev) != cudaSuccess) return;
+        bool done = false;
+        finalize(it->first, &done);
+        pending.pop_front();
+        return;
+    }
+}
+
 fer_status_t Session::make_job(std::vector<Temp> temps, uint64_t* out_job) {
     cudaEvent_t ev = nullptr;
+    if (spare_events.empty() && pending.size() >= 64) reclaim_oldest();
     if (!spare_events.empty()) {
         ev = spare_events.back();
         spare_events.pop_back();
@@ -172,6 +191,7 @@ fer_status_t Session::make_job(std::vector<Temp> temps, uint64_t* out_job) {
     Job& j = jobs[id];
     j.ev = ev;
     j.temps = std::move(temps);
+    pending.push_back(id);
     if (out_job) *out_job = id;
     return ok();
 }

@@ -20,6 +20,7 @@
 #include <cuda_runtime_api.h>
 
 #include <cstdint>
+#include <deque>
 #include <memory>
 #include <string>
 #include <unordered_map>
@@ -84,6 +85,7 @@ struct Session {
     std::unordered_map<uint64_t, Job> jobs;
     uint64_t next_job = 1;
     std::vector<cudaEvent_t> spare_events;
+    std::deque<uint64_t> pending;    // jobs not yet finalized, oldest first
     size_t live_bytes[2] = {0, 0};   // CUDA_MALLOC / MANAGED budget per tier
     uint32_t* dev_err = nullptr;     // device error word (cudaMalloc'd)
     std::unique_ptr<JitManager> jit;
@@ -106,6 +108,9 @@ struct Session {
     // Jobs: records completion of everything queued so far on the stream.
     fer_status_t make_job(std::vector<Temp> temps, uint64_t* out_job);
     fer_status_t finalize(uint64_t id, bool* done);
+    // Finalizes the oldest outstanding job if it has completed, returning its
+    // event to spare_events.
+    void reclaim_oldest();
 };
 
 // Validates a buffer descriptor (rank 1..4, known dtype, nonzero size).
