@@ -647,12 +647,73 @@ def subresults(s, capi, synth, torch, stream):
             for bx, by in wl.pairs:
                 s.free(bx)
                 s.free(by)
+    out["decode"] = decode_steps(s, capi, synth, torch)
     out["alloc_hook"] = hook_alloc_pairs(capi)
     tl = Tlsf(s, capi, synth).run(ops=100_000)
     out["tlsf"] = {"metric": Tlsf.metric, "value": tl["tlsf"]["alloc_p50_ns"], "unit": "ns", "results": tl,
                    "sample": "first 100k ops of the 1M-op trace (full trace: --workload tlsf)",
                    "reference_tlsf_host": Tlsf.cpu_reference(ops=100_000)}
     return out
+
+
+def decode_steps(s, capi, synth, torch, batch=64, prompt=512, steps=32):
+    """Incremental decoding on the benchmark model: prefill `prompt` tokens of
+    `batch` sequences into a KV cache (last-position logits), then `steps`
+    decode calls (one token per sequence each) timed with CUDA events on the
+    session stream. Roofline: the bytes a step must move (every weight once,
+    the KV cache read up to the current position, the new K/V written)
+    against the measured HBM copy rate."""
+    c = synth.TRANSFORMER
+    L, d, h, F, V = c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"]
+    m = capi.Transformer(s, L, d, h, F, V, batch * prompt, c["eps"])
+    m.init_weights(c["weight_seed"], 0.02)
+    u = synth.uniform01(c["token_seed"], batch * (prompt + steps + 4))
+    toks = np.minimum((u * V).astype(np.int32), V - 1).reshape(batch, prompt + steps + 4)
+    cache = m.kv_create(batch, prompt + steps + 4)
+    bt = s.alloc(capi.FER_DTYPE_I32, [batch, prompt])
+    s.upload(bt, np.ascontiguousarray(toks[:, :prompt]))
+    bl = s.alloc(capi.FER_DTYPE_F32, [batch, V])
+    dts = []
+    for k in range(steps + 4):
+        b = s.alloc(capi.FER_DTYPE_I32, [batch])
+        s.upload(b, np.ascontiguousarray(toks[:, prompt + k]))
+        dts.append(b)
+    ext = torch.cuda.ExternalStream(s.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.wait(m.prefill(cache, bt, bl))             # warm-up (kernels, JIT, pool)
+    torch.cuda.synchronize()
+    e0.record(ext)
+    s.wait(m.prefill(cache, bt, bl))
+    e1.record(ext)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    for k in range(4):
+        m.decode(cache, dts[k], bl)
+    torch.cuda.synchronize()
+    e0.record(ext)
+    for k in range(4, 4 + steps):
+        m.decode(cache, dts[k], bl)
+    e1.record(ext)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    errs = s.device_errors()
+    ctx = prompt + 4 + steps / 2                 # mean keys per step
+    kv_bytes = L * batch * d * 2 * 2 * (ctx + 1)   # K and V read (bf16) plus the new row
+    w_bytes = 2 * m.weight_elements()
+    pk, src = peak("hbm_gbs")
+    achieved = (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9
+    for b in dts + [bt, bl]:
+        s.free(b)
+    m.kv_destroy(cache)
+    m.close()
+    return {"metric": "decode tokens/s (one token per sequence per step)", "value": round(batch / (ms * 1e-3), 1),
+            "unit": "tokens/s", "ms_per_step": round(ms, 4), "batch": batch, "prompt": prompt, "steps": steps,
+            "prefill_ms": round(prefill_ms, 3), "prefill_tokens_per_s": round(batch * prompt / (prefill_ms * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk, "unit": "GB/s",
+                         "frac": round(achieved / pk, 4), "peak_source": src,
+                         "bytes_per_step": int(kv_bytes + w_bytes),
+                         "note": "every weight once + KV cache read to the current position + new K/V"},
+            "api": "fer_transformer_prefill / fer_transformer_decode", "device_error_bits": errs}
 
 
 def hook_alloc_pairs(capi, iters=50_000, cuda_iters=5_000, warmup=1_000, nbytes=65536):

@@ -280,6 +280,11 @@ CAPI_PROTOTYPES = {
     "fer_transformer_destroy": (S, [P, u64]),
     "fer_transformer_profile": (S, [P, u64, u32]),
     "fer_transformer_profile_read": (S, [P, u64, C.POINTER(fer_transformer_profile_t)]),
+    "fer_transformer_kv_create": (S, [P, u64, u32, u32, pu64]),
+    "fer_transformer_kv_destroy": (S, [P, u64, u64]),
+    "fer_transformer_kv_length": (S, [P, u64, u64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    "fer_transformer_prefill": (S, [P, u64, u64, u64, u64, pu64]),
+    "fer_transformer_decode": (S, [P, u64, u64, u64, u64, pu64]),
     "fer_session_device_errors": (S, [P, pu32, u8]),
     "fer_pool_get_stats": (S, [P, C.POINTER(fer_pool_stats_t)]),
     "fer_pool_alloc_raw": (S, [P, u64, C.POINTER(P)]),
@@ -552,6 +557,33 @@ class Transformer:
     def forward(self, tokens: int, logits: int) -> int:
         job = C.c_uint64()
         check("fer_transformer_forward", self.s.call("fer_transformer_forward", self.id, tokens, logits, C.byref(job)))
+        return job.value
+
+    def kv_create(self, max_batch: int, max_seq: int) -> int:
+        cid = C.c_uint64()
+        check("fer_transformer_kv_create",
+              self.s.call("fer_transformer_kv_create", self.id, max_batch, max_seq, C.byref(cid)))
+        return cid.value
+
+    def kv_destroy(self, cache: int) -> None:
+        check("fer_transformer_kv_destroy", self.s.call("fer_transformer_kv_destroy", self.id, cache))
+
+    def kv_length(self, cache: int) -> tuple[int, int]:
+        b, n = C.c_uint32(), C.c_uint32()
+        check("fer_transformer_kv_length", self.s.call("fer_transformer_kv_length", self.id, cache, C.byref(b),
+                                                       C.byref(n)))
+        return b.value, n.value
+
+    def prefill(self, cache: int, tokens: int, logits: int) -> int:
+        job = C.c_uint64()
+        check("fer_transformer_prefill",
+              self.s.call("fer_transformer_prefill", self.id, cache, tokens, logits, C.byref(job)))
+        return job.value
+
+    def decode(self, cache: int, tokens: int, logits: int) -> int:
+        job = C.c_uint64()
+        check("fer_transformer_decode", self.s.call("fer_transformer_decode", self.id, cache, tokens, logits,
+                                                    C.byref(job)))
         return job.value
 
     def profile(self, enable: bool) -> None:

@@ -147,6 +147,18 @@ cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* ou
 cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
                               float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s);
+size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K);
+cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi, int splits,
+                                    float* ws, size_t ws_bytes, uint32_t* err, cudaStream_t stream);
+cudaError_t fer_kv_store(const void* qkv, void* k_cache, void* v_cache, int B, int S, int d, int heads, int max_seq,
+                         int pos0, cudaStream_t s);
+size_t fer_attn_decode_scratch_floats(int B, int heads, int n_keys);
+cudaError_t fer_decode_kv_attention(const void* qkv_dec, void* k_cache, void* v_cache, void* out, float* scratch, int B,
+                                    int d, int heads, int max_seq, int* d_len, cudaStream_t s);
+cudaError_t fer_device_int_add(int* d_len, int v, cudaStream_t s);
+cudaError_t fer_device_int_set(int* d_len, int v, cudaStream_t s);
+cudaError_t fer_attn_decode(const void* qkv_dec, const void* k_cache, const void* v_cache, void* out, float* scratch,
+                            int B, int d, int heads, int max_seq, int n_keys, cudaStream_t s);
 cudaError_t fer_attn_causal_ex(const void* qkv, void* out, int B, int S, int d, int heads, int flags, uint32_t* err,
                                cudaStream_t s);
 }

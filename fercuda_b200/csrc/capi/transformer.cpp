@@ -20,9 +20,28 @@
 
 #include <cmath>
 #include <cstdlib>
+#include <unordered_map>
 #include <vector>
 
 namespace fer::capi {
+
+// Keys and values of up to max_batch sequences x max_seq positions, per
+// layer [max_batch][heads][max_seq][64] bf16 each (K block, then V block).
+struct KvCache {
+    uint32_t max_batch = 0, max_seq = 0;
+    uint32_t batch = 0, len = 0;     // set by prefill, len advanced by decode
+    uint16_t* kv = nullptr;          // layers x 2 x max_batch x heads x max_seq x 64
+    float* scratch = nullptr;        // decode attention chunk partials
+    float* gemm_ws = nullptr;        // split-K partials of the decode GEMMs
+    size_t gemm_ws_bytes = 0;
+    int* d_len = nullptr;            // device copy of len (position of the next token)
+    int* tok_stage = nullptr;        // decode tokens [max_batch] and logits [max_batch, vocab]
+    float* logit_stage = nullptr;    // at fixed addresses, so a captured step replays
+    cudaGraphExec_t graph = nullptr; // the decode step, captured on the second call with a batch
+    uint32_t graph_batch = 0;
+    uint32_t eager_batch = 0;
+    size_t layer_elems = 0;          // elements of one layer's K (or V) block
+};
 
 struct Transformer {
     fer_transformer_config_t cfg{};
@@ -56,6 +75,16 @@ struct Transformer {
     };
     std::vector<Graph> graphs;
     bool graphs_off = false;
+    std::unordered_map<uint64_t, KvCache> caches;
+
+    void free_cache(KvCache& kc) {
+        if (kc.graph) cudaGraphExecDestroy(kc.graph);
+        for (void* p : {static_cast<void*>(kc.kv), static_cast<void*>(kc.scratch), static_cast<void*>(kc.gemm_ws),
+                        static_cast<void*>(kc.d_len), static_cast<void*>(kc.tok_stage),
+                        static_cast<void*>(kc.logit_stage)})
+            if (p) gpu_hot_free(S->pool, p);
+        kc = KvCache{};
+    }
 
     cudaEvent_t event() {
         cudaEvent_t e = nullptr;
@@ -77,6 +106,7 @@ struct Transformer {
 
     ~Transformer() {
         if (!S) return;
+        for (auto& kv : caches) free_cache(kv.second);
         for (auto& g : graphs)
             if (g.exec) cudaGraphExecDestroy(g.exec);
         release_marks();
@@ -95,6 +125,7 @@ struct Transformer {
 }  // namespace fer::capi
 
 using fer::capi::Buffer;
+using fer::capi::KvCache;
 using fer::capi::Session;
 using fer::capi::Transformer;
 using fer::capi::internal;
@@ -336,6 +367,267 @@ fer_status_t fer_transformer_profile_read(fer_session_t* session, uint64_t model
     m->release_marks();
     *out = m->prof;
     return ok();
+}
+
+fer_status_t fer_transformer_kv_create(fer_session_t* session, uint64_t model, uint32_t max_batch, uint32_t max_seq,
+                                       uint64_t* out_cache) {
+    if (!session || !out_cache) return invalid("session or out_cache is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    if (max_batch == 0 || max_seq == 0) return invalid("kv cache needs max_batch > 0 and max_seq > 0");
+    const fer_transformer_config_t& c = m->cfg;
+    KvCache kc;
+    kc.max_batch = max_batch;
+    kc.max_seq = max_seq;
+    kc.layer_elems = static_cast<size_t>(max_batch) * c.d_model * max_seq;   // heads * 64 == d_model
+    kc.kv = static_cast<uint16_t*>(pool_alloc(S, kc.layer_elems * 2 * c.layers * sizeof(uint16_t)));
+    const size_t sf = fer_attn_decode_scratch_floats(static_cast<int>(max_batch), static_cast<int>(c.heads),
+                                                     static_cast<int>(max_seq));
+    kc.scratch = sf ? static_cast<float*>(pool_alloc(S, sf * sizeof(float))) : nullptr;
+    {
+        const int Mb = static_cast<int>(max_batch), d = static_cast<int>(c.d_model), F = static_cast<int>(c.ffn);
+        const int V = static_cast<int>(c.vocab);
+        const int shapes[5][2] = {{3 * d, d}, {d, d}, {F, d}, {d, F}, {V, d}};
+        for (const auto& nk : shapes) {
+            const size_t b = fer_gemm_splitk_workspace_bytes(Mb, nk[0], nk[1]);
+            if (b > kc.gemm_ws_bytes) kc.gemm_ws_bytes = b;
+        }
+        kc.gemm_ws = static_cast<float*>(pool_alloc(S, kc.gemm_ws_bytes));
+    }
+    kc.d_len = static_cast<int*>(pool_alloc(S, sizeof(int)));
+    kc.tok_stage = static_cast<int*>(pool_alloc(S, static_cast<size_t>(max_batch) * sizeof(int)));
+    kc.logit_stage = static_cast<float*>(pool_alloc(S, static_cast<size_t>(max_batch) * c.vocab * sizeof(float)));
+    if (!kc.kv || (sf && !kc.scratch) || !kc.gemm_ws || !kc.d_len || !kc.tok_stage || !kc.logit_stage) {
+        m->free_cache(kc);
+        return internal("kv cache allocation failed");
+    }
+    if (fer_device_int_set(kc.d_len, 0, S.stream) != cudaSuccess) {
+        cudaGetLastError();
+        m->free_cache(kc);
+        return internal("kernel launch failed");
+    }
+    const uint64_t id = S.next_model++;
+    m->caches.emplace(id, kc);
+    *out_cache = id;
+    return ok();
+}
+
+fer_status_t fer_transformer_kv_destroy(fer_session_t* session, uint64_t model, uint64_t cache) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    auto it = m->caches.find(cache);
+    if (it == m->caches.end()) return not_found("kv cache id not found");
+    cudaStreamSynchronize(S.stream);
+    m->free_cache(it->second);
+    m->caches.erase(it);
+    return ok();
+}
+
+fer_status_t fer_transformer_kv_length(fer_session_t* session, uint64_t model, uint64_t cache, uint32_t* out_batch,
+                                       uint32_t* out_len) {
+    if (!session) return invalid("session is null");
+    Transformer* m = find_model(session->impl, model);
+    if (!m) return not_found("model id not found");
+    auto it = m->caches.find(cache);
+    if (it == m->caches.end()) return not_found("kv cache id not found");
+    if (out_batch) *out_batch = it->second.batch;
+    if (out_len) *out_len = it->second.len;
+    return ok();
+}
+
+// The forward over a prompt that also fills the cache (positions 0 .. S-1 of
+// sequences 0 .. B-1). logits: f32 [B, S, vocab], or [B, vocab] for the last
+// position of each sequence only.
+fer_status_t fer_transformer_prefill(fer_session_t* session, uint64_t model, uint64_t cache, uint64_t tokens,
+                                     uint64_t logits, uint64_t* out_job_id) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    auto cit = m->caches.find(cache);
+    if (cit == m->caches.end()) return not_found("kv cache id not found");
+    KvCache& kc = cit->second;
+    const Buffer* tb = S.find(tokens);
+    const Buffer* lb = S.find(logits);
+    if (!tb || !lb) return not_found("buffer id not found");
+    if (tb->desc.dtype != FER_DTYPE_I32 || (tb->desc.rank != 1 && tb->desc.rank != 2))
+        return invalid("tokens must be i32 [batch, seq] or [seq]");
+    const int B = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[0]) : 1;
+    const int Sq = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[1]) : static_cast<int>(tb->desc.dims[0]);
+    const size_t T = static_cast<size_t>(B) * Sq;
+    const fer_transformer_config_t& c = m->cfg;
+    if (T > c.max_tokens) return invalid("batch * seq exceeds the model's max_tokens");
+    if (static_cast<uint32_t>(B) > kc.max_batch || static_cast<uint32_t>(Sq) > kc.max_seq)
+        return invalid("prompt exceeds the kv cache");
+    const bool last_only = lb->numel == static_cast<size_t>(B) * c.vocab;
+    if (lb->desc.dtype != FER_DTYPE_F32 || !(last_only || lb->numel == T * c.vocab))
+        return invalid("logits must be f32 [batch, seq, vocab] or [batch, vocab]");
+    const int d = static_cast<int>(c.d_model), F = static_cast<int>(c.ffn), V = static_cast<int>(c.vocab);
+    const int H = static_cast<int>(c.heads), Ti = static_cast<int>(T);
+    cudaStream_t st = S.stream;
+    uint32_t* err = S.dev_err;
+    const uint16_t* W = m->W;
+    cudaError_t e = fer_embed_f32(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, Ti, d, V, err, st);
+    for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
+        const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
+        const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
+        const float* g2 = m->ln + (4 * l + 2) * static_cast<size_t>(d);
+        const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
+        uint16_t* kcache = kc.kv + 2 * l * kc.layer_elems;
+        uint16_t* vcache = kcache + kc.layer_elems;
+        e = fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st);
+        if (e == cudaSuccess)
+            e = fer_gemm_bf16_tc_ex(m->a, W + m->off_qkv[l], m->qkv, nullptr, Ti, 3 * d, d, kEpiBF16, err, st);
+        if (e == cudaSuccess)
+            e = fer_kv_store(m->qkv, kcache, vcache, B, Sq, d, H, static_cast<int>(kc.max_seq), 0, st);
+        if (e == cudaSuccess) e = fer_attn_causal_ex(m->qkv, m->att, B, Sq, d, H, 0, err, st);
+        if (e == cudaSuccess)
+            e = fer_gemm_bf16_tc_ex(m->att, W + m->off_o[l], m->x, m->x, Ti, d, d, kEpiResidF32, err, st);
+        if (e == cudaSuccess) e = fer_ln_bf16(m->x, g2, b2, m->a, Ti, d, c.eps, st);
+        if (e == cudaSuccess)
+            e = fer_gemm_bf16_tc_ex(m->a, W + m->off_w1[l], m->hid, nullptr, Ti, F, d, kEpiGeluBF16, err, st);
+        if (e == cudaSuccess)
+            e = fer_gemm_bf16_tc_ex(m->hid, W + m->off_w2[l], m->x, m->x, Ti, d, F, kEpiResidF32, err, st);
+    }
+    const float* gf = m->ln + (4 * static_cast<size_t>(c.layers)) * d;
+    if (e == cudaSuccess) e = fer_ln_bf16(m->x, gf, gf + d, m->a, Ti, d, c.eps, st);
+    if (e == cudaSuccess) {
+        if (last_only) {
+            // rows b * S + S - 1 of the final-LN output, then the LM head on B rows
+            e = cudaMemcpy2DAsync(m->att, static_cast<size_t>(d) * 2, m->a + static_cast<size_t>(Sq - 1) * d,
+                                  static_cast<size_t>(Sq) * d * 2, static_cast<size_t>(d) * 2, B,
+                                  cudaMemcpyDeviceToDevice, st);
+            if (e == cudaSuccess)
+                e = fer_gemm_bf16_tc_ex(m->att, W + m->off_lm, lb->ptr, nullptr, B, V, d, kEpiF32, err, st);
+        } else {
+            e = fer_gemm_bf16_tc_ex(m->a, W + m->off_lm, lb->ptr, nullptr, Ti, V, d, kEpiF32, err, st);
+        }
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return internal("kernel launch failed");
+    }
+    if (fer_device_int_set(kc.d_len, Sq, st) != cudaSuccess) {
+        cudaGetLastError();
+        return internal("kernel launch failed");
+    }
+    kc.batch = static_cast<uint32_t>(B);
+    kc.len = static_cast<uint32_t>(Sq);
+    return S.make_job({}, out_job_id);
+}
+
+// One step of incremental decoding: token b (i32 [B]) appended to sequence
+// b of the cache at position len, attending to positions 0 .. len; logits
+// f32 [B, vocab]. The cache's len advances by one.
+fer_status_t fer_transformer_decode(fer_session_t* session, uint64_t model, uint64_t cache, uint64_t tokens,
+                                    uint64_t logits, uint64_t* out_job_id) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    auto cit = m->caches.find(cache);
+    if (cit == m->caches.end()) return not_found("kv cache id not found");
+    KvCache& kc = cit->second;
+    const Buffer* tb = S.find(tokens);
+    const Buffer* lb = S.find(logits);
+    if (!tb || !lb) return not_found("buffer id not found");
+    const fer_transformer_config_t& c = m->cfg;
+    if (tb->desc.dtype != FER_DTYPE_I32 || tb->numel != kc.batch || kc.batch == 0)
+        return invalid("decode takes one i32 token per sequence of the prefilled cache");
+    if (lb->desc.dtype != FER_DTYPE_F32 || lb->numel != static_cast<size_t>(kc.batch) * c.vocab)
+        return invalid("logits must be f32 [batch, vocab]");
+    if (kc.len >= kc.max_seq) return invalid("kv cache is full");
+    const int B = static_cast<int>(kc.batch);
+    const int d = static_cast<int>(c.d_model), F = static_cast<int>(c.ffn), V = static_cast<int>(c.vocab);
+    const int H = static_cast<int>(c.heads), max_seq = static_cast<int>(kc.max_seq);
+    cudaStream_t st = S.stream;
+    uint32_t* err = S.dev_err;
+    const uint16_t* W = m->W;
+    // M = B rows: split-K GEMMs, so that a short batch still spreads each
+    // weight matrix over the whole GPU. The position lives in kc.d_len on
+    // the device and every buffer address is fixed, so the whole step is
+    // captured once per batch size and replayed (first call eager).
+    auto gemm = [&](const void* a, const void* b, void* cc, int N, int K, int epi) {
+        return fer_gemm_bf16_tc_splitk(a, b, cc, B, N, K, epi, 0, kc.gemm_ws, kc.gemm_ws_bytes, err, st);
+    };
+    cudaError_t e = cudaSuccess;
+    auto issue = [&]() {
+        e = fer_embed_f32(kc.tok_stage, W + m->off_emb, m->x, B, d, V, err, st);
+        for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
+            const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
+            const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
+            const float* g2 = m->ln + (4 * l + 2) * static_cast<size_t>(d);
+            const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
+            uint16_t* kcache = kc.kv + 2 * l * kc.layer_elems;
+            uint16_t* vcache = kcache + kc.layer_elems;
+            e = fer_ln_bf16(m->x, g1, b1, m->a, B, d, c.eps, st);
+            if (e == cudaSuccess) e = gemm(m->a, W + m->off_qkv[l], m->qkv, 3 * d, d, kEpiBF16);
+            if (e == cudaSuccess)
+                e = fer_decode_kv_attention(m->qkv, kcache, vcache, m->att, kc.scratch, B, d, H, max_seq, kc.d_len, st);
+            if (e == cudaSuccess) e = gemm(m->att, W + m->off_o[l], m->x, d, d, kEpiResidF32);
+            if (e == cudaSuccess) e = fer_ln_bf16(m->x, g2, b2, m->a, B, d, c.eps, st);
+            if (e == cudaSuccess) e = gemm(m->a, W + m->off_w1[l], m->hid, F, d, kEpiGeluBF16);
+            if (e == cudaSuccess) e = gemm(m->hid, W + m->off_w2[l], m->x, d, F, kEpiResidF32);
+        }
+        const float* gf = m->ln + (4 * static_cast<size_t>(c.layers)) * d;
+        if (e == cudaSuccess) e = fer_ln_bf16(m->x, gf, gf + d, m->a, B, d, c.eps, st);
+        if (e == cudaSuccess) e = gemm(m->a, W + m->off_lm, kc.logit_stage, V, d, kEpiF32);
+        if (e == cudaSuccess) e = fer_device_int_add(kc.d_len, 1, st);
+    };
+    e = cudaMemcpyAsync(kc.tok_stage, tb->ptr, static_cast<size_t>(B) * sizeof(int), cudaMemcpyDeviceToDevice, st);
+    static int graphs_env = -1;
+    if (graphs_env < 0) {
+        const char* ev = std::getenv("FERCUDA_XFMR_GRAPH");
+        graphs_env = (ev && ev[0] == '0') ? 0 : 1;
+    }
+    const bool use_graph = graphs_env && !m->profiling && !m->graphs_off;
+    if (e == cudaSuccess) {
+        if (use_graph && kc.graph && kc.graph_batch == kc.batch) {
+            e = cudaGraphLaunch(kc.graph, st);
+        } else if (use_graph && kc.eager_batch == kc.batch) {
+            if (kc.graph) {
+                cudaGraphExecDestroy(kc.graph);
+                kc.graph = nullptr;
+            }
+            cudaGraph_t graph = nullptr;
+            if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+                issue();
+                const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+                if (e == cudaSuccess && ce == cudaSuccess && graph &&
+                    cudaGraphInstantiate(&kc.graph, graph, 0) != cudaSuccess)
+                    kc.graph = nullptr;
+                if (graph) cudaGraphDestroy(graph);
+                if (e != cudaSuccess || ce != cudaSuccess || !kc.graph) {
+                    cudaGetLastError();
+                    m->graphs_off = true;   // stay eager from now on
+                    kc.graph = nullptr;
+                    issue();
+                } else {
+                    kc.graph_batch = kc.batch;
+                    e = cudaGraphLaunch(kc.graph, st);
+                }
+            } else {
+                cudaGetLastError();
+                m->graphs_off = true;
+                issue();
+            }
+        } else {
+            issue();
+            kc.eager_batch = kc.batch;
+        }
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(lb->ptr, kc.logit_stage, static_cast<size_t>(B) * V * sizeof(float),
+                            cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return internal("kernel launch failed");
+    }
+    kc.len += 1;
+    return S.make_job({}, out_job_id);
 }
 
 fer_status_t fer_transformer_destroy(fer_session_t* session, uint64_t model) {

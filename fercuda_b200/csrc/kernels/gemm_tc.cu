@@ -190,7 +190,8 @@ __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, uint32_t* err) {
+                        const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, int splits, int kps,
+                        uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -199,6 +200,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int num_k = (K + BK - 1) / BK;
+    // Split-K (splits > 1): job t covers k-blocks [kps * split, ...) of tile
+    // t % num_tiles and stores its f32 partial at rows split * num_m * BM +
+    // ... of C; splits == 1 is the plain GEMM (one job per tile, all of K).
+    const int num_jobs = num_tiles * splits;
+    auto job_k = [&](int t, int* kb0, int* nk) {
+        const int split = t / num_tiles;
+        *kb0 = split * kps;
+        const int left = num_k - *kb0;
+        *nk = left < kps ? left : kps;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -230,10 +241,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer
         int it = 0;
-        for (int t = blockIdx.x; t < num_tiles && !warp_flag(abort_flag); t += gridDim.x) {
-            int mb, nb;
-            tile_coords(t, num_m, num_n, &mb, &nb);
-            for (int kt = 0; kt < num_k; ++kt, ++it) {
+        for (int t = blockIdx.x; t < num_jobs && !warp_flag(abort_flag); t += gridDim.x) {
+            int mb, nb, kb0, nk;
+            tile_coords(t % num_tiles, num_m, num_n, &mb, &nb);
+            job_k(t, &kb0, &nk);
+            for (int kt = 0; kt < nk; ++kt, ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
                 if (!__all_sync(0xffffffffu, mbar_wait(&bars.empty[s], ph ^ 1u))) {
@@ -245,10 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint8_t* sa = smem + s * STAGE_BYTES;
                     uint8_t* sb = sa + A_BYTES;
                     mbar_arrive_expect_tx(&bars.full[s], STAGE_BYTES);
-                    tma_load_2d(sa, &tmA, kt * BK, mb * BM, &bars.full[s]);
+                    tma_load_2d(sa, &tmA, (kb0 + kt) * BK, mb * BM, &bars.full[s]);
 #pragma unroll
                     for (int c = 0; c < BN / 64; ++c)
-                        tma_load_2d(sb + c * (BK * 128), &tmB, nb * BN + c * 64, kt * BK, &bars.full[s]);
+                        tma_load_2d(sb + c * (BK * 128), &tmB, nb * BN + c * 64, (kb0 + kt) * BK, &bars.full[s]);
                 }
                 __syncwarp();
             }
@@ -256,7 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (lane 0 issues)
         int it = 0, local = 0;
-        for (int t = blockIdx.x; t < num_tiles && !warp_flag(abort_flag); t += gridDim.x, ++local) {
+        for (int t = blockIdx.x; t < num_jobs && !warp_flag(abort_flag); t += gridDim.x, ++local) {
+            int kb0, nk;
+            job_k(t, &kb0, &nk);
             const int buf = local & 1;
             const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
             if (!__all_sync(0xffffffffu, mbar_wait(&bars.acc_empty[buf], acc_ph ^ 1u))) {
@@ -267,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
             bool ok = true;
-            for (int kt = 0; kt < num_k; ++kt, ++it) {
+            for (int kt = 0; kt < nk; ++kt, ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
                 if (!__all_sync(0xffffffffu, mbar_wait(&bars.full[s], ph))) {
@@ -305,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int chunk_cols = f32_out ? 32 : 64;            // one 128-byte box row
         const int n_chunks = (BN / 2) / chunk_cols;
         int local = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+        for (int t = blockIdx.x; t < num_jobs; t += gridDim.x, ++local) {
             const int buf = local & 1;
             const uint32_t acc_ph = static_cast<uint32_t>(local >> 1) & 1u;
             const bool got = __all_sync(0xffffffffu, mbar_wait(&bars.acc_full[buf], acc_ph));
@@ -316,8 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             int mb, nb;
-            tile_coords(t, num_m, num_n, &mb, &nb);
-            const int row0 = mb * BM + q * 32;
+            tile_coords(t % num_tiles, num_m, num_n, &mb, &nb);
+            const int row_in = mb * BM + q * 32;                          // row within this job's M rows
+            const int row0 = (t / num_tiles) * num_m * BM + row_in;       // row of C (split block offset)
             const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(buf * BN + half * (BN / 2));
 #pragma unroll 1
@@ -355,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 const int col0 = nb * BN + half * (BN / 2) + c * chunk_cols;
-                if (lane == 0 && row0 < M && col0 < N) {
+                if (lane == 0 && row_in < M && col0 < N) {
                     if (epi == kEpiResidF32) tma_reduce_add_2d(&tmC, stage, col0, row0);
                     else tma_store_2d(&tmC, stage, col0, row0);
                     bulk_commit();
@@ -795,7 +810,148 @@ extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, mc, M, N, K, epi, err);
+    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, mc, M, N, K, epi, 1, (K + BK - 1) / BK,
+                                                                 err);
+    return cudaGetLastError();
+}
+
+namespace {
+
+// out = epilogue(sum over splits s = 0, 1, ... of part[s * mpad + m][n]) for
+// m < M: the partials are added in split order, so the result is the same
+// bits on every run.
+__global__ void __launch_bounds__(256) splitk_reduce(const float* __restrict__ part, void* __restrict__ out, int M,
+                                                     int N, int mpad, int splits, int epi) {
+    const size_t total4 = static_cast<size_t>(M) * N / 4;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total4; i += stride) {
+        const size_t e = i * 4;
+        const size_t m = e / N, n = e % N;
+        const size_t slab = static_cast<size_t>(mpad) * N;   // floats between consecutive splits
+        const float4* src = reinterpret_cast<const float4*>(part + m * N + n);
+        float4 acc = src[0];
+        int sp = 1;
+        // four splits' loads in flight, added in split order
+        for (; sp + 3 < splits; sp += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = src[(sp + u) * slab / 4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                acc.x += v[u].x;
+                acc.y += v[u].y;
+                acc.z += v[u].z;
+                acc.w += v[u].w;
+            }
+        }
+        for (; sp < splits; ++sp) {
+            const float4 v = src[sp * slab / 4];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        if (epi == kEpiF32) {
+            reinterpret_cast<float4*>(out)[i] = acc;
+        } else if (epi == kEpiResidF32) {
+            float4 r = reinterpret_cast<float4*>(out)[i];
+            r.x += acc.x;
+            r.y += acc.y;
+            r.z += acc.z;
+            r.w += acc.w;
+            reinterpret_cast<float4*>(out)[i] = r;
+        } else {
+            if (epi == kEpiGeluBF16) {
+                acc.x = gelu_erf(acc.x);
+                acc.y = gelu_erf(acc.y);
+                acc.z = gelu_erf(acc.z);
+                acc.w = gelu_erf(acc.w);
+            }
+            uint2 w;
+            w.x = pack_bf16x2(acc.x, acc.y);
+            w.y = pack_bf16x2(acc.z, acc.w);
+            reinterpret_cast<uint2*>(out)[i] = w;
+        }
+    }
+}
+
+}  // namespace
+
+namespace {
+
+size_t splitk_bytes(int M, int N, int splits) {
+    const size_t mpad = static_cast<size_t>((M + BM - 1) / BM) * BM;
+    return static_cast<size_t>(splits) * mpad * N * sizeof(float);
+}
+
+// Splits actually used: `want` (<= 0: enough jobs for one per SM), at most
+// one per 64-deep k-block, reduced until the partials fit ws_bytes; every
+// split gets at least one block. 0 when even one split does not fit.
+int splitk_plan(int M, int N, int K, int want, size_t ws_bytes, int* kps_out) {
+    const int num_k = (K + BK - 1) / BK;
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    int splits = want > 0 ? want : (sm_count() + tiles - 1) / tiles;
+    if (splits > num_k) splits = num_k;
+    if (splits < 1) splits = 1;
+    while (splits > 1 && splitk_bytes(M, N, splits) > ws_bytes) --splits;
+    if (splitk_bytes(M, N, splits) > ws_bytes) return 0;
+    const int kps = (num_k + splits - 1) / splits;
+    *kps_out = kps;
+    return (num_k + kps - 1) / kps;
+}
+
+}  // namespace
+
+// Workspace bytes for fer_gemm_bf16_tc_splitk with the automatic split count.
+extern "C" size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K) {
+    int kps = 0;
+    const int splits = splitk_plan(M, N, K, 0, static_cast<size_t>(-1), &kps);
+    return splitk_bytes(M, N, splits);
+}
+
+// Split-K tensor-core GEMM for short M (decode steps): K is divided into
+// ranges of whole 64-deep blocks computed by separate CTAs into an f32
+// workspace, then added in range order by one more kernel that applies the
+// epilogue (epi as fer_gemm_bf16_tc_ex; for epi 3 the residual is c itself).
+// Deterministic, but the additions are grouped differently from
+// fer_gemm_bf16_tc_ex, so the low bits differ from it. splits <= 0 picks a
+// count that gives every SM one job; the count is reduced until the
+// partials fit ws_bytes (cudaErrorInvalidValue if one split does not).
+extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi,
+                                               int splits, float* ws, size_t ws_bytes, uint32_t* err,
+                                               cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || (K % 8) || (N % 8) || epi < kEpiF32 || epi > kEpiResidF32 || !ws)
+        return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c) |
+         reinterpret_cast<uintptr_t>(ws)) & 15u)
+        return cudaErrorInvalidValue;
+    int kps = 0;
+    splits = splitk_plan(M, N, K, splits, ws_bytes, &kps);
+    if (splits == 0) return cudaErrorInvalidValue;
+    const int num_m = (M + BM - 1) / BM;
+    const int tiles = num_m * ((N + BN - 1) / BN);
+    const int mpad = num_m * BM;
+    CUtensorMap ma, mb, mc;
+    if (!make_map(&ma, a, static_cast<uint64_t>(M), static_cast<uint64_t>(K), BM) ||
+        !make_map(&mb, b, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK) ||
+        !make_map(&mc, ws, static_cast<uint64_t>(splits) * mpad, static_cast<uint64_t>(N), 32,
+                  CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+        return cudaErrorInvalidValue;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int jobs = tiles * splits;
+    const int grid = jobs < sm_count() ? jobs : sm_count();
+    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, mc, M, N, K, kEpiF32, splits, kps, err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t total4 = static_cast<size_t>(M) * N / 4;
+    size_t g = (total4 + 255) / 256;
+    if (g > static_cast<size_t>(sm_count()) * 8) g = static_cast<size_t>(sm_count()) * 8;
+    splitk_reduce<<<static_cast<unsigned>(g), 256, 0, stream>>>(ws, c, M, N, mpad, splits, epi);
     return cudaGetLastError();
 }
 

@@ -139,6 +139,29 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
                                      uint64_t* out_job_id);
 fer_status_t fer_transformer_destroy(fer_session_t* session, uint64_t model);
 
+/* ---- KV cache and incremental decoding --------------------------------------
+ * A KV cache of a model holds, per layer, the keys and values of up to
+ * max_batch sequences x max_seq positions (bf16, [max_batch][heads][max_seq][64]
+ * for K and for V), from the session pool. prefill runs the forward over a
+ * prompt (tokens i32 [batch, seq]) and stores its keys and values at
+ * positions 0 .. seq-1; logits f32 [batch, seq, vocab], or [batch, vocab] for
+ * each sequence's last position. decode appends one token per sequence
+ * (tokens i32 [batch], batch as prefilled) at position len, attends to
+ * positions 0 .. len and writes logits f32 [batch, vocab]; len advances by
+ * one. Decode attention is split over 256-position chunks and combined in
+ * chunk order: bit-identical run to run. The cache ids share the model id
+ * space; destroying the model frees its caches. */
+fer_status_t fer_transformer_kv_create(fer_session_t* session, uint64_t model, uint32_t max_batch, uint32_t max_seq,
+                                       uint64_t* out_cache);
+fer_status_t fer_transformer_kv_destroy(fer_session_t* session, uint64_t model, uint64_t cache);
+/* Sequences and positions currently held (both 0 before the first prefill). */
+fer_status_t fer_transformer_kv_length(fer_session_t* session, uint64_t model, uint64_t cache, uint32_t* out_batch,
+                                       uint32_t* out_len);
+fer_status_t fer_transformer_prefill(fer_session_t* session, uint64_t model, uint64_t cache, uint64_t tokens,
+                                     uint64_t logits, uint64_t* out_job_id);
+fer_status_t fer_transformer_decode(fer_session_t* session, uint64_t model, uint64_t cache, uint64_t tokens,
+                                    uint64_t logits, uint64_t* out_job_id);
+
 /* Per-kernel-class timing of forwards: while enabled, every forward records a
  * CUDA event pair around each of its launches on the session stream; reading
  * synchronises the stream and sums the elapsed times. Enabling resets. */

@@ -36,6 +36,15 @@ cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c, const flo
 /* out_dtype: 0 f32, 2 bf16 (fer_buffer_dtype_t codes). */
 cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K, uint32_t out_dtype,
                              uint32_t* err, cudaStream_t stream);
+/* Split-K form for short M (decode steps): K split into ranges of 64-deep
+ * blocks computed by separate CTAs into the f32 workspace `ws`, added in range
+ * order by a second kernel that applies `epi` (for epi 3 the residual is c).
+ * Deterministic; the additions are grouped differently from
+ * fer_gemm_bf16_tc_ex. splits <= 0: two jobs per SM, reduced to fit ws_bytes.
+ * fer_gemm_splitk_workspace_bytes: ws needed for the automatic count. */
+size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K);
+cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi, int splits,
+                                    float* ws, size_t ws_bytes, uint32_t* err, cudaStream_t stream);
 /* 0 (default): 2-CTA cluster kernel for M > 128; 1: single-CTA kernel. Both
  * give the same bits. Process-wide. */
 void fer_gemm_tc_set_mode(int mode);
@@ -96,6 +105,27 @@ cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int
 /* The tcgen05 kernel alone: cudaErrorNotSupported where it does not apply. */
 cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int S, int d, int heads, uint32_t* err,
                                cudaStream_t stream);
+/* KV cache (per layer [max_batch][heads][max_seq][64] bf16, K and V blocks):
+ * fer_kv_store copies the K and V parts of qkv [B*S, 3d] (rows b*S + s) to
+ * positions pos0 + s of sequences b. fer_attn_decode: one query per sequence
+ * (the Q part of row b of qkv_dec [B, 3d]) against positions 0 .. n_keys-1,
+ * out [B, d] bf16; split into 256-position chunks combined in chunk order,
+ * scratch of fer_attn_decode_scratch_floats(B, heads, n_keys) floats (0: none
+ * needed). head_dim 64. */
+cudaError_t fer_kv_store(const void* qkv, void* k_cache, void* v_cache, int B, int S, int d, int heads, int max_seq,
+                         int pos0, cudaStream_t s);
+size_t fer_attn_decode_scratch_floats(int B, int heads, int n_keys);
+cudaError_t fer_attn_decode(const void* qkv_dec, const void* k_cache, const void* v_cache, void* out, float* scratch,
+                            int B, int d, int heads, int max_seq, int n_keys, cudaStream_t s);
+/* The decode step's cache store + attention with the position in device
+ * memory (*d_len = position of the new token, advanced by the caller with
+ * fer_device_int_add): launch arguments never change between steps, so the
+ * step can be captured in a CUDA graph and replayed. scratch as
+ * fer_attn_decode_scratch_floats(B, heads, max_seq). */
+cudaError_t fer_decode_kv_attention(const void* qkv_dec, void* k_cache, void* v_cache, void* out, float* scratch, int B,
+                                    int d, int heads, int max_seq, int* d_len, cudaStream_t s);
+cudaError_t fer_device_int_add(int* d_len, int v, cudaStream_t s);
+cudaError_t fer_device_int_set(int* d_len, int v, cudaStream_t s);
 /* Per-token layer norm, x f32 [T, d] -> out bf16, d one of 128, 256, ..., 4096. */
 cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* out, int T, int d, float eps,
                         cudaStream_t s);

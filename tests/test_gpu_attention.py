@@ -53,7 +53,8 @@ def make_qkv(B, S, heads, seed, scale=1.0):
     return (torch.randn(B * S, 3 * heads * 64, generator=g, device="cuda") * scale).bfloat16()
 
 
-@pytest.mark.parametrize("B,S,heads,scale", [(2, 512, 4, 1.0), (1, 128, 2, 1.0), (3, 256, 16, 2.0), (1, 640, 1, 4.0)])
+@pytest.mark.parametrize("B,S,heads,scale", [(2, 512, 4, 1.0), (1, 128, 2, 1.0), (3, 256, 16, 2.0), (1, 640, 1, 4.0),
+                                           (1, 2048, 2, 1.0), (1, 4096, 1, 1.0)])
 def test_tcgen05_kernel_vs_reference_and_mma_sync(B, S, heads, scale):
     qkv = make_qkv(B, S, heads, 7 + S, scale)
     ref = reference(qkv, B, S, heads)
