@@ -153,12 +153,13 @@ cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M
 cudaError_t fer_kv_store(const void* qkv, void* k_cache, void* v_cache, int B, int S, int d, int heads, int max_seq,
                          int pos0, cudaStream_t s);
 size_t fer_attn_decode_scratch_floats(int B, int heads, int n_keys);
-cudaError_t fer_decode_kv_attention(const void* qkv_dec, void* k_cache, void* v_cache, void* out, float* scratch, int B,
-                                    int d, int heads, int max_seq, int* d_len, cudaStream_t s);
+cudaError_t fer_decode_kv_attention(const void* qkv_dec, void* k_cache, void* v_cache, void* out, float* scratch,
+                                    int* counters, int B, int d, int heads, int max_seq, int* d_len, uint32_t* err,
+                                    cudaStream_t s);
 cudaError_t fer_device_int_add(int* d_len, int v, cudaStream_t s);
 cudaError_t fer_device_int_set(int* d_len, int v, cudaStream_t s);
 cudaError_t fer_attn_decode(const void* qkv_dec, const void* k_cache, const void* v_cache, void* out, float* scratch,
-                            int B, int d, int heads, int max_seq, int n_keys, cudaStream_t s);
+                            int B, int d, int heads, int max_seq, int n_keys, uint32_t* err, cudaStream_t s);
 cudaError_t fer_attn_causal_ex(const void* qkv, void* out, int B, int S, int d, int heads, int flags, uint32_t* err,
                                cudaStream_t s);
 }

@@ -32,6 +32,7 @@ struct KvCache {
     uint32_t batch = 0, len = 0;     // set by prefill, len advanced by decode
     uint16_t* kv = nullptr;          // layers x 2 x max_batch x heads x max_seq x 64
     float* scratch = nullptr;        // decode attention chunk partials
+    int* attn_counters = nullptr;    // decode attention: chunks done per (sequence, head)
     float* gemm_ws = nullptr;        // split-K partials of the decode GEMMs
     size_t gemm_ws_bytes = 0;
     int* d_len = nullptr;            // device copy of len (position of the next token)
@@ -79,7 +80,8 @@ struct Transformer {
 
     void free_cache(KvCache& kc) {
         if (kc.graph) cudaGraphExecDestroy(kc.graph);
-        for (void* p : {static_cast<void*>(kc.kv), static_cast<void*>(kc.scratch), static_cast<void*>(kc.gemm_ws),
+        for (void* p : {static_cast<void*>(kc.kv), static_cast<void*>(kc.scratch),
+                        static_cast<void*>(kc.attn_counters), static_cast<void*>(kc.gemm_ws),
                         static_cast<void*>(kc.d_len), static_cast<void*>(kc.tok_stage),
                         static_cast<void*>(kc.logit_stage)})
             if (p) gpu_hot_free(S->pool, p);
@@ -385,6 +387,8 @@ fer_status_t fer_transformer_kv_create(fer_session_t* session, uint64_t model, u
     const size_t sf = fer_attn_decode_scratch_floats(static_cast<int>(max_batch), static_cast<int>(c.heads),
                                                      static_cast<int>(max_seq));
     kc.scratch = sf ? static_cast<float*>(pool_alloc(S, sf * sizeof(float))) : nullptr;
+    const size_t n_counters = static_cast<size_t>(max_batch) * c.heads;
+    kc.attn_counters = static_cast<int*>(pool_alloc(S, n_counters * sizeof(int)));
     {
         const int Mb = static_cast<int>(max_batch), d = static_cast<int>(c.d_model), F = static_cast<int>(c.ffn);
         const int V = static_cast<int>(c.vocab);
@@ -398,11 +402,13 @@ fer_status_t fer_transformer_kv_create(fer_session_t* session, uint64_t model, u
     kc.d_len = static_cast<int*>(pool_alloc(S, sizeof(int)));
     kc.tok_stage = static_cast<int*>(pool_alloc(S, static_cast<size_t>(max_batch) * sizeof(int)));
     kc.logit_stage = static_cast<float*>(pool_alloc(S, static_cast<size_t>(max_batch) * c.vocab * sizeof(float)));
-    if (!kc.kv || (sf && !kc.scratch) || !kc.gemm_ws || !kc.d_len || !kc.tok_stage || !kc.logit_stage) {
+    if (!kc.kv || (sf && !kc.scratch) || !kc.attn_counters || !kc.gemm_ws || !kc.d_len || !kc.tok_stage ||
+        !kc.logit_stage) {
         m->free_cache(kc);
         return internal("kv cache allocation failed");
     }
-    if (fer_device_int_set(kc.d_len, 0, S.stream) != cudaSuccess) {
+    if (fer_device_int_set(kc.d_len, 0, S.stream) != cudaSuccess ||
+        cudaMemsetAsync(kc.attn_counters, 0, n_counters * sizeof(int), S.stream) != cudaSuccess) {
         cudaGetLastError();
         m->free_cache(kc);
         return internal("kernel launch failed");
@@ -566,7 +572,8 @@ fer_status_t fer_transformer_decode(fer_session_t* session, uint64_t model, uint
             e = fer_ln_bf16(m->x, g1, b1, m->a, B, d, c.eps, st);
             if (e == cudaSuccess) e = gemm(m->a, W + m->off_qkv[l], m->qkv, 3 * d, d, kEpiBF16);
             if (e == cudaSuccess)
-                e = fer_decode_kv_attention(m->qkv, kcache, vcache, m->att, kc.scratch, B, d, H, max_seq, kc.d_len, st);
+                e = fer_decode_kv_attention(m->qkv, kcache, vcache, m->att, kc.scratch, kc.attn_counters, B, d, H,
+                                            max_seq, kc.d_len, err, st);
             if (e == cudaSuccess) e = gemm(m->att, W + m->off_o[l], m->x, d, d, kEpiResidF32);
             if (e == cudaSuccess) e = fer_ln_bf16(m->x, g2, b2, m->a, B, d, c.eps, st);
             if (e == cudaSuccess) e = gemm(m->a, W + m->off_w1[l], m->hid, F, d, kEpiGeluBF16);

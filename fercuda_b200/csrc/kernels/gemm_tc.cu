@@ -30,6 +30,7 @@
 // Every wait is bounded (about one second); on timeout the kernel records an
 // error bit, stops issuing work, releases tensor memory and returns.
 // No TMA multicast is used anywhere.
+#include "pdl.cuh"
 #include "sm100_util.cuh"
 
 #include <cuda.h>
@@ -184,14 +185,96 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
                  : "memory");
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t nclusters_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 16 bytes of another CTA's shared memory (address from map_to_rank).
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// Split-K epilogue for four consecutive outputs (float4 index i4 of the
+// row-major M x N output; N % 4 == 0): the sum over splits, already added
+// in split order, through the epilogue of fer_gemm_bf16_tc_ex.
+__device__ __forceinline__ void splitk_store4(float4 acc, void* __restrict__ out, size_t i4, int epi) {
+    if (epi == kEpiF32) {
+        reinterpret_cast<float4*>(out)[i4] = acc;
+    } else if (epi == kEpiResidF32) {
+        float4 r = reinterpret_cast<float4*>(out)[i4];
+        r.x += acc.x;
+        r.y += acc.y;
+        r.z += acc.z;
+        r.w += acc.w;
+        reinterpret_cast<float4*>(out)[i4] = r;
+    } else {
+        if (epi == kEpiGeluBF16) {
+            acc.x = gelu_erf(acc.x);
+            acc.y = gelu_erf(acc.y);
+            acc.z = gelu_erf(acc.z);
+            acc.w = gelu_erf(acc.w);
+        }
+        uint2 w;
+        w.x = pack_bf16x2(acc.x, acc.y);
+        w.y = pack_bf16x2(acc.z, acc.w);
+        reinterpret_cast<uint2*>(out)[i4] = w;
+    }
+}
+
+__device__ __forceinline__ void add4(float4& a, const float4& v) {
+    a.x += v.x;
+    a.y += v.y;
+    a.z += v.z;
+    a.w += v.w;
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// f32 partial tile of the cluster split-K mode: row stride in floats (the
+// 4-float pad puts 8 consecutive rows' 16-byte pieces in distinct banks).
+constexpr int kPartStride = BN + 4;
+static_assert(BM * kPartStride * 4 <= STAGES * STAGE_BYTES, "partial tile must fit the stage ring");
+
+// kCluster: split-K through distributed shared memory. The grid is launched
+// in clusters of `splits` CTAs; the CTAs of one cluster share one output tile
+// (job t: tile t / splits, split t % splits = rank in the cluster), each
+// computes its K range into TMEM and copies it to its shared memory, and
+// after a cluster barrier CTA r adds the partials of all splits, in split
+// order, for its 1/splits share of the tile and stores them through the
+// epilogue directly to `out` (row-major M x N). No workspace, no second
+// kernel; the same bits as the workspace form with the same split count.
+template <bool kCluster>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, int splits, int kps,
-                        uint32_t* err) {
+                        void* __restrict__ out, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -204,8 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // t % num_tiles and stores its f32 partial at rows split * num_m * BM +
     // ... of C; splits == 1 is the plain GEMM (one job per tile, all of K).
     const int num_jobs = num_tiles * splits;
+    auto job_tile = [&](int t) { return kCluster ? t / splits : t % num_tiles; };
+    auto job_split = [&](int t) { return kCluster ? t % splits : t / num_tiles; };
     auto job_k = [&](int t, int* kb0, int* nk) {
-        const int split = t / num_tiles;
+        const int split = job_split(t);
         *kb0 = split * kps;
         const int left = num_k - *kb0;
         *nk = left < kps ? left : kps;
@@ -234,6 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars.tmem_base;
+    // Setup above touches no global memory; under programmatic launch it
+    // overlaps the previous kernel.
+    fer::dev::pdl_begin();
 
     volatile int* abort_flag = &bars.abort_flag;
     // Each role loop is run by its whole warp (waits voted across the warp,
@@ -243,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int it = 0;
         for (int t = blockIdx.x; t < num_jobs && !warp_flag(abort_flag); t += gridDim.x) {
             int mb, nb, kb0, nk;
-            tile_coords(t % num_tiles, num_m, num_n, &mb, &nb);
+            tile_coords(job_tile(t), num_m, num_n, &mb, &nb);
             job_k(t, &kb0, &nk);
             for (int kt = 0; kt < nk; ++kt, ++it) {
                 const int s = it % STAGES;
@@ -330,11 +418,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             int mb, nb;
-            tile_coords(t % num_tiles, num_m, num_n, &mb, &nb);
+            tile_coords(job_tile(t), num_m, num_n, &mb, &nb);
             const int row_in = mb * BM + q * 32;                          // row within this job's M rows
-            const int row0 = (t / num_tiles) * num_m * BM + row_in;       // row of C (split block offset)
+            const int row0 = job_split(t) * num_m * BM + row_in;          // row of C (split block offset)
             const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(buf * BN + half * (BN / 2));
+            if constexpr (kCluster) {
+                // f32 partial rows -> this CTA's shared memory (the stage
+                // ring is idle: every load of the one job has been consumed
+                // by MMAs that completed before acc_full)
+                const int r = q * 32 + lane;
+                const bool live = row_in + lane < M;
+                const uint32_t prow = smem_addr(smem) + static_cast<uint32_t>((r * kPartStride + half * (BN / 2)) * 4);
+#pragma unroll 1
+                for (int c = 0; c < (BN / 2) / 32; ++c) {
+                    uint32_t w[32];
+                    tmem_ld32(tbase + c * 32, w);
+                    if (c == (BN / 2) / 32 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
+                    }
+                    if (live) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + (c * 32 + 4 * j) * 4),
+                                         "r"(w[4 * j]), "r"(w[4 * j + 1]), "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                                         : "memory");
+                    }
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int c = 0; c < n_chunks; ++c) {
                 uint32_t w[32];
@@ -382,6 +496,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     }
 
+    if constexpr (kCluster) {
+        cluster_sync_all();   // every split's partial is in its CTA's shared memory
+        const int t = blockIdx.x;
+        int mb, nb;
+        tile_coords(job_tile(t), num_m, num_n, &mb, &nb);
+        const int rank = job_split(t);
+        const int rows = M - mb * BM < BM ? M - mb * BM : BM;
+        const int total = rows * (BN / 4);                     // float4 pieces of the tile's live rows
+        const int per = (total + splits - 1) / splits;
+        const int f_end = (rank + 1) * per < total ? (rank + 1) * per : total;
+        const uint32_t pbase = smem_addr(smem);
+        for (int f = rank * per + static_cast<int>(threadIdx.x); f < f_end; f += kThreads) {
+            const int r = f / (BN / 4), c4 = f % (BN / 4);
+            const int col = nb * BN + c4 * 4;
+            if (col >= N) continue;
+            const uint32_t off = pbase + static_cast<uint32_t>((r * kPartStride + c4 * 4) * 4);
+            float4 acc = ld_cluster_f4(map_to_rank(off, 0));
+            int sp = 1;
+            // four splits' loads in flight, added in split order
+            for (; sp + 3 < splits; sp += 4) {
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = ld_cluster_f4(map_to_rank(off, static_cast<uint32_t>(sp + u)));
+#pragma unroll
+                for (int u = 0; u < 4; ++u) add4(acc, v[u]);
+            }
+            for (; sp < splits; ++sp) add4(acc, ld_cluster_f4(map_to_rank(off, static_cast<uint32_t>(sp))));
+            splitk_store4(acc, out, (static_cast<size_t>(mb * BM + r) * N + col) / 4, epi);
+        }
+        cluster_sync_all();   // no CTA exits while its partial is still being read
+    }
+
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -420,30 +566,6 @@ struct Bars2 {
     int abort_flag;
 };
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t nclusters_x() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-    return r;
-}
-// Address of the same shared-memory object in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster) {
     asm volatile(
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
@@ -804,15 +926,17 @@ extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c
     }
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, mc, M, N, K, epi, 1, (K + BK - 1) / BK,
-                                                                 err);
-    return cudaGetLastError();
+    const cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES,
+                                                stream, ma, mb, mc, M, N, K, epi, 1, (K + BK - 1) / BK,
+                                                static_cast<void*>(nullptr), err);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 namespace {
@@ -822,6 +946,7 @@ namespace {
 // bits on every run.
 __global__ void __launch_bounds__(256) splitk_reduce(const float* __restrict__ part, void* __restrict__ out, int M,
                                                      int N, int mpad, int splits, int epi) {
+    fer::dev::pdl_begin();
     const size_t total4 = static_cast<size_t>(M) * N / 4;
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total4; i += stride) {
@@ -837,41 +962,10 @@ __global__ void __launch_bounds__(256) splitk_reduce(const float* __restrict__ p
 #pragma unroll
             for (int u = 0; u < 4; ++u) v[u] = src[(sp + u) * slab / 4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                acc.x += v[u].x;
-                acc.y += v[u].y;
-                acc.z += v[u].z;
-                acc.w += v[u].w;
-            }
+            for (int u = 0; u < 4; ++u) add4(acc, v[u]);
         }
-        for (; sp < splits; ++sp) {
-            const float4 v = src[sp * slab / 4];
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
-        }
-        if (epi == kEpiF32) {
-            reinterpret_cast<float4*>(out)[i] = acc;
-        } else if (epi == kEpiResidF32) {
-            float4 r = reinterpret_cast<float4*>(out)[i];
-            r.x += acc.x;
-            r.y += acc.y;
-            r.z += acc.z;
-            r.w += acc.w;
-            reinterpret_cast<float4*>(out)[i] = r;
-        } else {
-            if (epi == kEpiGeluBF16) {
-                acc.x = gelu_erf(acc.x);
-                acc.y = gelu_erf(acc.y);
-                acc.z = gelu_erf(acc.z);
-                acc.w = gelu_erf(acc.w);
-            }
-            uint2 w;
-            w.x = pack_bf16x2(acc.x, acc.y);
-            w.y = pack_bf16x2(acc.z, acc.w);
-            reinterpret_cast<uint2*>(out)[i] = w;
-        }
+        for (; sp < splits; ++sp) add4(acc, src[sp * slab / 4]);
+        splitk_store4(acc, out, i, epi);
     }
 }
 
@@ -909,14 +1003,99 @@ extern "C" size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K) {
     return splitk_bytes(M, N, splits);
 }
 
+namespace {
+
+// Largest cluster of split-K CTAs allowed (FERCUDA_SPLITK_CLUSTER: 0 turns
+// the cluster form off, 2..16 caps the cluster size; default 16).
+int csplit_cap() {
+    static const int cap = [] {
+        const char* e = std::getenv("FERCUDA_SPLITK_CLUSTER");
+        if (!e || !*e) return 16;
+        const int v = std::atoi(e);
+        return v < 2 ? 0 : (v > 16 ? 16 : v);
+    }();
+    return cap;
+}
+
+// Clusters of `size` CTAs of the cluster split-K kernel that can be resident
+// at once (0: none), queried once per size.
+int csplit_max_clusters(int size) {
+    static int cache[17] = {};
+    if (cache[size] == 0) {
+        int n = 0;
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_BYTES);
+        if (e == cudaSuccess && size > 8)
+            e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(static_cast<unsigned>(size * 16));
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = SMEM_BYTES;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = static_cast<unsigned>(size);
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            e = cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tc_kernel<true>, &cfg);
+        }
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        cache[size] = n > 0 ? n : -1;
+    }
+    return cache[size] > 0 ? cache[size] : 0;
+}
+
+// Cluster split-K plan: the largest split count S <= 16 (each split whole
+// 64-deep k-blocks, S = ceil(num_k / ceil(num_k / S))) whose clusters of S
+// CTAs all fit on the GPU at once, one cluster per output tile. 1: no split
+// fits (the plain kernel runs); 0: the cluster form is off.
+int csplit_plan(int M, int N, int K, int* kps_out) {
+    const int cap = csplit_cap();
+    const int num_k = (K + BK - 1) / BK;
+    *kps_out = num_k;
+    if (cap == 0) return 0;
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    for (int S = num_k < cap ? num_k : cap; S >= 2; --S) {
+        const int kps = (num_k + S - 1) / S;
+        if ((num_k + kps - 1) / kps != S) continue;
+        if (tiles <= csplit_max_clusters(S)) {
+            *kps_out = kps;
+            return S;
+        }
+    }
+    return 1;
+}
+
+}  // namespace
+
+// Split count the automatic fer_gemm_bf16_tc_splitk uses in its cluster
+// form: >= 2 clusters of that many CTAs, 1 the single-pass kernel, 0 the
+// cluster form is switched off (FERCUDA_SPLITK_CLUSTER=0).
+extern "C" int fer_gemm_splitk_cluster_splits(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    int kps = 0;
+    return csplit_plan(M, N, K, &kps);
+}
+
 // Split-K tensor-core GEMM for short M (decode steps): K is divided into
-// ranges of whole 64-deep blocks computed by separate CTAs into an f32
-// workspace, then added in range order by one more kernel that applies the
-// epilogue (epi as fer_gemm_bf16_tc_ex; for epi 3 the residual is c itself).
-// Deterministic, but the additions are grouped differently from
-// fer_gemm_bf16_tc_ex, so the low bits differ from it. splits <= 0 picks a
-// count that gives every SM one job; the count is reduced until the
-// partials fit ws_bytes (cudaErrorInvalidValue if one split does not).
+// ranges of whole 64-deep blocks computed by separate CTAs, and the f32
+// partials are added in range order before the epilogue (epi as
+// fer_gemm_bf16_tc_ex; for epi 3 the residual is c itself). Deterministic,
+// but the additions are grouped differently from fer_gemm_bf16_tc_ex, so the
+// low bits differ from it.
+// splits <= 0 (automatic): the cluster form (fer_gemm_splitk_cluster_splits)
+// adds the partials through distributed shared memory inside one kernel, or
+// the single-pass kernel runs when no split fits; ws is not touched.
+// splits > 0, or the cluster form switched off: the partials go to the f32
+// workspace ws and one more kernel adds them; the count is reduced until the
+// partials fit ws_bytes (cudaErrorInvalidValue if one split does not), and
+// with the cluster form off, splits <= 0 gives every SM one job. Both forms
+// give the same bits for the same split count.
 extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi,
                                                int splits, float* ws, size_t ws_bytes, uint32_t* err,
                                                cudaStream_t stream) {
@@ -926,6 +1105,36 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
          reinterpret_cast<uintptr_t>(ws)) & 15u)
         return cudaErrorInvalidValue;
     int kps = 0;
+    if (splits <= 0) {
+        const int cs = csplit_plan(M, N, K, &kps);
+        if (cs == 1) return fer_gemm_bf16_tc_ex(a, b, c, epi == kEpiResidF32 ? static_cast<const float*>(c) : nullptr,
+                                                M, N, K, epi, err, stream);
+        if (cs >= 2) {
+            CUtensorMap ma, mb;
+            if (!make_map(&ma, a, static_cast<uint64_t>(M), static_cast<uint64_t>(K), BM) ||
+                !make_map(&mb, b, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK))
+                return cudaErrorInvalidValue;
+            const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(static_cast<unsigned>(tiles * cs));
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = SMEM_BYTES;
+            cfg.stream = stream;
+            cudaLaunchAttribute at[2];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = static_cast<unsigned>(cs);
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[1].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = fer::host::pdl_enabled() ? 2 : 1;
+            // the C map is not used by the cluster form
+            const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<true>, ma, mb, ma, M, N, K, epi, cs,
+                                                     kps, c, err);
+            return e != cudaSuccess ? e : cudaGetLastError();
+        }
+    }
     splits = splitk_plan(M, N, K, splits, ws_bytes, &kps);
     if (splits == 0) return cudaErrorInvalidValue;
     const int num_m = (M + BM - 1) / BM;
@@ -939,20 +1148,24 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
         return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     const int jobs = tiles * splits;
     const int grid = jobs < sm_count() ? jobs : sm_count();
-    gemm_bf16_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(ma, mb, mc, M, N, K, kEpiF32, splits, kps, err);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES, stream,
+                                          ma, mb, mc, M, N, K, static_cast<int>(kEpiF32), splits, kps,
+                                          static_cast<void*>(nullptr), err);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const size_t total4 = static_cast<size_t>(M) * N / 4;
     size_t g = (total4 + 255) / 256;
     if (g > static_cast<size_t>(sm_count()) * 8) g = static_cast<size_t>(sm_count()) * 8;
-    splitk_reduce<<<static_cast<unsigned>(g), 256, 0, stream>>>(ws, c, M, N, mpad, splits, epi);
-    return cudaGetLastError();
+    e = fer::host::launch_pdl(splitk_reduce, dim3(static_cast<unsigned>(g)), dim3(256), 0, stream,
+                              static_cast<const float*>(ws), c, M, N, mpad, splits, epi);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // out_dtype: 0 = f32, 2 = bf16 (fer_buffer_dtype_t codes).

@@ -1,0 +1,53 @@
+// Programmatic dependent launch (PDL).
+//
+// A kernel launched with the programmatic-serialization attribute may be
+// scheduled while the kernel before it on the stream is still running, so
+// its launch and prologue overlap that kernel's tail. Such a kernel calls
+// pdl_begin() before its first global-memory access: griddepcontrol.wait
+// returns once the preceding kernel has completed and its writes are
+// visible; launch_dependents then lets the next kernel be scheduled. Without
+// a programmatic predecessor both are no-ops, so the kernels stay correct
+// under plain launches. FERCUDA_PDL=0 launches without the attribute.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <utility>
+
+namespace fer::dev {
+
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
+}  // namespace fer::dev
+
+namespace fer::host {
+
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("FERCUDA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Launches a kernel that begins with pdl_begin(), with the PDL attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+}  // namespace fer::host

@@ -3,18 +3,22 @@
 //
 // KV cache layout, per layer: K and V each [max_batch][heads][max_seq][64]
 // bf16, so the history of one (sequence, head) is one contiguous run of
-// 128-byte rows: a warp reading 32 consecutive positions reads 4 KB of
-// contiguous memory.
+// 128-byte rows, and one chunk of kChunk positions is one contiguous run of
+// kChunk * 128 bytes.
 //
 // Decode attention for one new query per sequence: positions [0, len] of
 // each (sequence, head) are split into chunks of kChunk; one CTA per
-// (sequence, head, chunk) computes the chunk's scores q.k / 8, their maximum
-// m, p = exp(s - m), l = sum p and o = sum p v in f32, in a fixed order; a
-// second kernel combines the chunks in chunk order (max, rescale, sum) and
-// writes o / l as bf16. With one chunk the first kernel writes the result.
-// Every reduction order depends only on len, so results are bit-identical
-// run to run.
+// (sequence, head, chunk) computes the scores q.k / 8 (each thread one key,
+// a 128-byte row, all its loads in flight at once), their maximum m, p = exp(s - m), l = sum p and o = sum p v
+// in f32, in a fixed order, and writes (m, l, o) of the chunk. The last CTA
+// of a (sequence, head) to finish (a counter in device memory) combines the
+// chunks in chunk order (max, rescale, sum) and writes o / l as bf16; with
+// one chunk the CTA writes the result itself. Which CTA combines does not
+// change the arithmetic, and every reduction order depends only on len, so
+// results are bit-identical run to run.
+#include "pdl.cuh"
 #include "sm100_util.cuh"
+#include "tmap.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -25,8 +29,12 @@ namespace {
 
 using bf16 = __nv_bfloat16;
 constexpr int HD = 64;
-constexpr int kChunk = 256;      // positions per CTA
-constexpr int kThreads = 128;
+constexpr int kSub = 32;         // positions per pipeline stage
+constexpr int kStages = 3;
+constexpr int kRowBytes = HD * 2;                        // one cached position, 128 bytes
+constexpr int kStageBytes = 2 * kSub * kRowBytes;        // K rows then V rows, 8 KB
+constexpr int kSmemBytes = kStages * kStageBytes + 1024; // + slack for 1024-byte alignment
+constexpr int kThreads = 128;                            // 32 key slots x 4 lanes
 
 // K and V of rows t = b * S + s (s < S) of qkv [B*S, 3d] into the caches at
 // position pos0 + s. One thread per 16-byte piece.
@@ -47,26 +55,10 @@ __global__ void kv_store(const bf16* __restrict__ qkv, bf16* __restrict__ kc, bf
     }
 }
 
-// One row per sequence (S = 1) at the position held in device memory, so a
-// captured decode step replays unchanged as the position advances.
-__global__ void kv_store_at(const bf16* __restrict__ qkv, bf16* __restrict__ kc, bf16* __restrict__ vc, int B, int d,
-                            int heads, int max_seq, const int* __restrict__ d_pos) {
-    const int pos = *d_pos;
-    const int per_row = 2 * d / 8;
-    const int total = B * per_row;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const int b = i / per_row, j = i % per_row;
-        const int kv = j / (d / 8), w = j % (d / 8);
-        const int h = w / 8, part = w % 8;
-        if (pos < 0 || pos >= max_seq) return;
-        const uint4 val = *reinterpret_cast<const uint4*>(qkv + static_cast<size_t>(b) * 3 * d + d + kv * d + h * HD +
-                                                          part * 8);
-        bf16* dst = (kv ? vc : kc) + ((static_cast<size_t>(b) * heads + h) * max_seq + pos) * HD + part * 8;
-        *reinterpret_cast<uint4*>(dst) = val;
-    }
+__global__ void add_to_int(int* p, int v) {
+    fer::dev::pdl_begin();
+    *p += v;
 }
-
-__global__ void add_to_int(int* p, int v) { *p += v; }
 __global__ void set_int(int* p, int v) { *p = v; }
 
 __device__ __forceinline__ float block_max(float v, float* sh) {
@@ -89,121 +81,248 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
     return r;
 }
 
-// grid (B * heads, chunks). q: row b of qkv_dec [B, 3d]. part: per (b, h,
-// chunk) the chunk's m, l and o[64] (66 floats), unused when chunks == 1.
-__global__ void __launch_bounds__(kThreads) decode_attn_chunk(const bf16* __restrict__ qkv_dec,
-                                                              const bf16* __restrict__ kc,
-                                                              const bf16* __restrict__ vc, bf16* __restrict__ out,
-                                                              float* __restrict__ part, int d, int heads,
-                                                              int max_seq, int n_keys_arg,
-                                                              const int* __restrict__ d_len) {
-    // d_len given: keys 0 .. *d_len (the new token included), and the grid
-    // is sized for the cache's largest chunk count
-    const int n_keys = d_len ? *d_len + 1 : n_keys_arg;
-    const int chunks = (n_keys + kChunk - 1) / kChunk;
-    if (static_cast<int>(blockIdx.y) >= chunks || n_keys > max_seq) return;
-    __shared__ float q[HD];
-    __shared__ float p[kChunk];
-    __shared__ float red[4];
-    __shared__ float ogrp[16][HD];
-    const int bh = blockIdx.x, b = bh / heads, h = bh % heads;
+__device__ __forceinline__ void tma_load_rows(void* dst, const CUtensorMap* map, int row, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            fer::dev::smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(fer::dev::smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Address of 16-byte piece c of row r in a 128-byte-swizzled stage.
+__device__ __forceinline__ int swz(int r, int c) { return r * kRowBytes + ((c ^ (r & 7)) << 4); }
+
+// Keys [k0, k0 + nk) of one (sequence, head) in stages of kSub positions:
+// tmK / tmV are maps over the cache rows (box 64 x kSub, 128-byte swizzle),
+// so a stage of K and V is two TMA loads; kStages stages in flight.
+// Thread t = 4 * slot + qt owns key slot `slot` of every stage and dims
+// 16 qt .. 16 qt + 15: it adds its part of q.k (two 16-byte pieces, in dim
+// order), the four parts are added by a fixed butterfly (every lane of the
+// slot gets the same score), and the slot keeps its own running maximum m,
+// sum l and o[16 dims] (online softmax, rescaled when m grows). At the end
+// the 32 slots are combined in slot order.
+//
+// grid (B * heads, G). With G > 1 the keys are split into chunks of
+// clen = ceil(n_keys / G) rounded up to kSub (CTAs past the last chunk
+// return); each chunk CTA writes (m, l, o[64]) to part, and the last CTA of
+// a (sequence, head) to finish (counters, zero before the launch and left
+// zero) combines the chunks in chunk order. With one chunk the CTA writes
+// the result. d_len given (a decode step): keys 0 .. *d_len, where position
+// *d_len is the new token, whose K / V rows come from qkv_dec (stored into
+// the caches here, and into the stage in place of the loaded rows); d_len
+// null: keys 0 .. n_keys_arg - 1, all from the caches.
+__global__ void __launch_bounds__(kThreads) decode_attn(const __grid_constant__ CUtensorMap tmK,
+                                                        const __grid_constant__ CUtensorMap tmV,
+                                                        const bf16* __restrict__ qkv_dec, bf16* __restrict__ kc,
+                                                        bf16* __restrict__ vc, bf16* __restrict__ out,
+                                                        float* __restrict__ part, int* __restrict__ counters, int d,
+                                                        int heads, int max_seq, int n_keys_arg,
+                                                        const int* __restrict__ d_len, uint32_t* err) {
+    using namespace fer::dev;
+    pdl_begin();
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full[kStages];
+    __shared__ int is_last;
+    const int pos = d_len ? *d_len : -1;
+    const int n_keys = d_len ? pos + 1 : n_keys_arg;
+    if (n_keys <= 0 || n_keys > max_seq) return;          // refused by the host
+    const int G = static_cast<int>(gridDim.y);
+    const int clen = ((n_keys + G - 1) / G + kSub - 1) / kSub * kSub;
+    const int chunks = (n_keys + clen - 1) / clen;
     const int chunk = blockIdx.y;
-    const int k0 = chunk * kChunk;
-    const int nk = n_keys - k0 < kChunk ? n_keys - k0 : kChunk;
-    const int t = threadIdx.x;
-    if (t < HD) q[t] = __bfloat162float(qkv_dec[static_cast<size_t>(b) * 3 * d + h * HD + t]) * 0.125f;
+    if (chunk >= chunks) return;
+    const int bh = blockIdx.x, b = bh / heads, h = bh % heads;
+    const int k0 = chunk * clen;
+    const int nk = n_keys - k0 < clen ? n_keys - k0 : clen;
+    const int nsub = (nk + kSub - 1) / kSub;
+    const int j_new = d_len ? pos - k0 : -1;              // chunk-local index of the new key, when in [0, nk)
+    const int row0 = bh * max_seq + k0;
+    uint8_t* st = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int t = threadIdx.x, slot = t >> 2, qt = t & 3;
+
+    if (t == 0) {
+        for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
+        fence_mbar_init();
+    }
     __syncthreads();
-    const bf16* kb = kc + (static_cast<size_t>(bh) * max_seq + k0) * HD;
-    const bf16* vb = vc + (static_cast<size_t>(bh) * max_seq + k0) * HD;
-    // scores: thread t takes keys t, t + 128
-    float smax = -INFINITY;
-    for (int j = t; j < nk; j += kThreads) {
-        const uint4* row = reinterpret_cast<const uint4*>(kb + static_cast<size_t>(j) * HD);
+    auto issue = [&](int i) {
+        uint8_t* sk = st + (i % kStages) * kStageBytes;
+        mbar_arrive_expect_tx(&full[i % kStages], kStageBytes);
+        tma_load_rows(sk, &tmK, row0 + i * kSub, &full[i % kStages]);
+        tma_load_rows(sk + kSub * kRowBytes, &tmV, row0 + i * kSub, &full[i % kStages]);
+    };
+    if (t == 0)
+        for (int i = 0; i < kStages && i < nsub; ++i) issue(i);
+
+    const bf16* qrow = qkv_dec + static_cast<size_t>(b) * 3 * d;
+    float qr[16];
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(qrow + h * HD + 16 * qt + e));
+        qr[e] = f.x * 0.125f;
+        qr[e + 1] = f.y * 0.125f;
+    }
+    const bool has_new = j_new >= 0 && j_new < nk;
+    uint4 new_piece = make_uint4(0, 0, 0, 0);
+    if (has_new && t < 16) {
+        // t < 8: K piece t, else V piece t - 8; also stored into the cache
+        const int kv = t >> 3, piece = t & 7;
+        new_piece = *reinterpret_cast<const uint4*>(qrow + d + kv * d + h * HD + piece * 8);
+        *reinterpret_cast<uint4*>((kv ? vc : kc) + (static_cast<size_t>(row0) + j_new) * HD + piece * 8) = new_piece;
+    }
+
+    float m = -INFINITY, l = 0.0f, acc[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+    for (int i = 0; i < nsub; ++i) {
+        const int s_i = i % kStages;
+        const bool ok = mbar_wait(&full[s_i], static_cast<uint32_t>(i / kStages) & 1u);
+        if (!__syncthreads_and(ok)) {
+            if (t == 0) {
+                report(err, kErrTimeoutLoad);
+                // bounded: let the loads this CTA issued (sub-chunks i .. i + kStages - 1) land before it exits
+                for (int k = i; k < i + kStages && k < nsub; ++k)
+                    mbar_wait(&full[k % kStages], static_cast<uint32_t>(k / kStages) & 1u);
+            }
+            return;
+        }
+        uint8_t* sk = st + s_i * kStageBytes;
+        uint8_t* sv = sk + kSub * kRowBytes;
+        const int jn = j_new - i * kSub;
+        if (has_new && jn >= 0 && jn < kSub) {            // the same branch for the whole CTA
+            if (t < 16) *reinterpret_cast<uint4*>((t < 8 ? sk : sv) + swz(jn, t & 7)) = new_piece;
+            __syncthreads();
+        }
+        const int j = i * kSub + slot;
         float s = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint4 u = row[c];
+        for (int cc = 0; cc < 2; ++cc) {
+            const uint4 u = lds128(sk + swz(slot, 2 * qt + cc));
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
-                s = fmaf(q[c * 8 + 2 * e], f.x, s);
-                s = fmaf(q[c * 8 + 2 * e + 1], f.y, s);
+                s = fmaf(qr[8 * cc + 2 * e], f.x, s);
+                s = fmaf(qr[8 * cc + 2 * e + 1], f.y, s);
             }
         }
-        p[j] = s;
-        smax = fmaxf(smax, s);
-    }
-    const float m = block_max(smax, red);
-    float lsum = 0.0f;
-    for (int j = t; j < nk; j += kThreads) {
-        const float e = __expf(p[j] - m);
-        p[j] = e;
-        lsum += e;
-    }
-    const float l = block_sum(lsum, red);   // also orders the p[] writes before the reads below
-    // o = sum_j p_j v[j]: thread t takes dims 8 * (t % 8) .. +7 (one 16-byte
-    // piece of a V row) over keys j = t / 8, t / 8 + 16, ...; the 16 key
-    // groups are then added in group order
-    const int dg = t % 8, kg = t / 8;
-    float acc[8];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if (j < nk) {
+            if (s > m) {
+                const float alpha = __expf(m - s);
+                l *= alpha;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-    for (int j = kg; j < nk; j += 16) {
-        const uint4 u = reinterpret_cast<const uint4*>(vb + static_cast<size_t>(j) * HD)[dg];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-        const float pj = p[j];
+                for (int e = 0; e < 16; ++e) acc[e] *= alpha;
+                m = s;
+            }
+            const float pj = __expf(s - m);
+            l += pj;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
-            acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
-            acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
+            for (int cc = 0; cc < 2; ++cc) {
+                const uint4 u = lds128(sv + swz(slot, 2 * qt + cc));
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+                    acc[8 * cc + 2 * e] = fmaf(pj, f.x, acc[8 * cc + 2 * e]);
+                    acc[8 * cc + 2 * e + 1] = fmaf(pj, f.y, acc[8 * cc + 2 * e + 1]);
+                }
+            }
         }
+        if (has_new) fence_proxy_async_smem();            // a generic write may precede the stage's next load
+        __syncthreads();                                  // stage s_i fully read
+        if (t == 0 && i + kStages < nsub) issue(i + kStages);
     }
+
+    // combine the 32 slots in slot order (the stage ring is idle now)
+    float* so = reinterpret_cast<float*>(st);              // [32][64]
+    float* sm = so + 32 * HD;                              // [32]
+    float* sl = sm + 32;                                   // [32]
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ogrp[kg][dg * 8 + e] = acc[e];
+    for (int e = 0; e < 16; e += 4)
+        *reinterpret_cast<float4*>(so + slot * HD + 16 * qt + e) = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+    if (qt == 0) {
+        sm[slot] = m;
+        sl[slot] = l;
+    }
     __syncthreads();
+    bf16* dst = out + static_cast<size_t>(b) * d + h * HD;
+    float M = -INFINITY, L = 0.0f, o = 0.0f;
     if (t < HD) {
-        const int i = t;
-        float o = ogrp[0][i];
-#pragma unroll
-        for (int g = 1; g < 16; ++g) o += ogrp[g][i];
-        if (chunks == 1) {
-            out[static_cast<size_t>(b) * d + h * HD + i] = __float2bfloat16(o / l);
-        } else {
-            float* pp = part + (static_cast<size_t>(bh) * chunks + chunk) * (HD + 2);
-            pp[2 + i] = o;
-            if (i == 0) {
-                pp[0] = m;
-                pp[1] = l;
-            }
+        for (int k = 0; k < 32; ++k) M = fmaxf(M, sm[k]);
+        for (int k = 0; k < 32; ++k) {
+            const float w = __expf(sm[k] - M);             // 0 for a slot that saw no key
+            L = fmaf(sl[k], w, L);
+            o = fmaf(so[k * HD + t], w, o);
         }
+    }
+    if (chunks == 1) {
+        if (t < HD) dst[t] = __float2bfloat16(o / L);
+        return;
+    }
+    float* pp = part + static_cast<size_t>(bh) * chunks * (HD + 2);
+    if (t < HD) {
+        pp[chunk * (HD + 2) + 2 + t] = o;
+        if (t == 0) {
+            pp[chunk * (HD + 2)] = M;
+            pp[chunk * (HD + 2) + 1] = L;
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    if (t == 0) is_last = atomicAdd(&counters[bh], 1) == chunks - 1;
+    __syncthreads();
+    if (!is_last) return;
+    // every chunk of (b, h) is written: combine them in chunk order
+    __threadfence();
+    if (t < HD) {
+        float Mc = -INFINITY;
+        for (int c = 0; c < chunks; ++c) Mc = fmaxf(Mc, __ldcg(pp + c * (HD + 2)));
+        float Lc = 0.0f, oc = 0.0f;
+        for (int c = 0; c < chunks; ++c) {
+            const float* qc = pp + c * (HD + 2);
+            const float w = __expf(__ldcg(qc) - Mc);
+            Lc = fmaf(__ldcg(qc + 1), w, Lc);
+            oc = fmaf(__ldcg(qc + 2 + t), w, oc);
+        }
+        dst[t] = __float2bfloat16(oc / Lc);
+        if (t == 0) counters[bh] = 0;
     }
 }
 
-// One warp per (b, h): chunks combined in chunk order.
-__global__ void decode_attn_combine(const float* __restrict__ part, bf16* __restrict__ out, int d, int heads,
-                                    int chunks_arg, int BH, const int* __restrict__ d_len) {
-    const int chunks = d_len ? (*d_len + 1 + kChunk - 1) / kChunk : chunks_arg;
-    if (chunks <= 1) return;     // the chunk kernel wrote the result
-    const int lane = threadIdx.x & 31;
-    const int bh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (bh >= BH) return;
-    const float* pp = part + static_cast<size_t>(bh) * chunks * (HD + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < chunks; ++c) M = fmaxf(M, pp[c * (HD + 2)]);
-    float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
-    for (int c = 0; c < chunks; ++c) {
-        const float* q = pp + c * (HD + 2);
-        const float w = __expf(q[0] - M);
-        L = fmaf(q[1], w, L);
-        o0 = fmaf(q[2 + lane], w, o0);
-        o1 = fmaf(q[2 + 32 + lane], w, o1);
-    }
-    const int b = bh / heads, h = bh % heads;
-    bf16* dst = out + static_cast<size_t>(b) * d + h * HD;
-    dst[lane] = __float2bfloat16(o0 / L);
-    dst[32 + lane] = __float2bfloat16(o1 / L);
+int sm_count() {
+    static int n = [] {
+        int dev = 0, v = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
+    return n;
+}
+
+// Chunks per (sequence, head): enough CTAs for one full wave when B * heads
+// alone does not fill the GPU, never more than one per kSub keys.
+int grid_chunks(int BH, int max_keys, int resident_per_sm) {
+    const int by_keys = (max_keys + kSub - 1) / kSub;
+    int g = sm_count() * resident_per_sm / BH;
+    if (g > by_keys) g = by_keys;
+    return g < 1 ? 1 : g;
+}
+
+int resident_per_sm() {
+    static int r = [] {
+        int v = 0;
+        if (cudaFuncSetAttribute(decode_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, decode_attn, kThreads, kSmemBytes) != cudaSuccess) {
+            cudaGetLastError();
+            v = 0;
+        }
+        return v;
+    }();
+    return r;
 }
 
 }  // namespace
@@ -221,63 +340,99 @@ extern "C" cudaError_t fer_kv_store(const void* qkv, void* k_cache, void* v_cach
     return cudaGetLastError();
 }
 
-// Floats of scratch fer_attn_decode needs for B sequences and n_keys keys.
+// Floats of scratch fer_attn_decode needs for B sequences and n_keys keys
+// (and fer_decode_kv_attention for any batch up to B): chunk partials of 66
+// floats, as many as B' * heads * G can reach for B' <= B (G <= 16 * SMs /
+// (B' * heads) when it exceeds one, at most 16 CTAs being resident per SM),
+// then one counter per (sequence, head). 0 when no launch splits the keys.
 extern "C" size_t fer_attn_decode_scratch_floats(int B, int heads, int n_keys) {
-    const int chunks = (n_keys + kChunk - 1) / kChunk;
-    return chunks > 1 ? static_cast<size_t>(B) * heads * chunks * (HD + 2) : 0;
+    if (B <= 0 || heads <= 0 || n_keys <= 0) return 0;
+    const size_t BH = static_cast<size_t>(B) * heads;
+    const size_t by_keys = static_cast<size_t>((n_keys + kSub - 1) / kSub);
+    if (by_keys <= 1) return 0;
+    size_t parts = static_cast<size_t>(sm_count()) * 16;
+    if (parts < BH) parts = BH;
+    if (parts > BH * by_keys) parts = BH * by_keys;
+    return parts * (HD + 2) + BH;
 }
 
+namespace {
+
+cudaError_t launch_decode_attn(const void* qkv_dec, void* k_cache, void* v_cache, void* out, float* scratch,
+                               int* counters, int B, int d, int heads, int max_seq, int n_keys, int max_keys,
+                               const int* d_len, uint32_t* err, bool pdl, cudaStream_t s) {
+    const int res = resident_per_sm();
+    if (res <= 0) return cudaErrorInvalidConfiguration;
+    const int BH = B * heads;
+    const int G = grid_chunks(BH, max_keys, res);
+    if (G > 1 && (!scratch || !counters)) return cudaErrorInvalidValue;
+    CUtensorMap mk, mv;
+    const unsigned long long rows = static_cast<unsigned long long>(BH) * max_seq;
+    if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u ||
+        !fer::host::map_rows64_bf16(&mk, k_cache, rows, kSub) || !fer::host::map_rows64_bf16(&mv, v_cache, rows, kSub))
+        return cudaErrorInvalidValue;
+    const dim3 grid(static_cast<unsigned>(BH), static_cast<unsigned>(G));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl && fer::host::pdl_enabled() ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attn, mk, mv, static_cast<const bf16*>(qkv_dec),
+                                             static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache),
+                                             static_cast<bf16*>(out), scratch, counters, d, heads, max_seq, n_keys,
+                                             d_len, err);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+}  // namespace
+
 // One query per sequence (row b of qkv_dec [B, 3d], its Q part) against keys
-// / values 0 .. n_keys - 1 of the caches; out [B, d] bf16.
+// / values 0 .. n_keys - 1 of the caches; out [B, d] bf16. scratch:
+// fer_attn_decode_scratch_floats(B, heads, n_keys) floats (its counters are
+// cleared here, on the stream).
 extern "C" cudaError_t fer_attn_decode(const void* qkv_dec, const void* k_cache, const void* v_cache, void* out,
                                        float* scratch, int B, int d, int heads, int max_seq, int n_keys,
-                                       cudaStream_t s) {
+                                       uint32_t* err, cudaStream_t s) {
     if (B <= 0 || d != heads * HD || n_keys <= 0 || n_keys > max_seq) return cudaErrorInvalidValue;
-    const int chunks = (n_keys + kChunk - 1) / kChunk;
-    if (chunks > 1 && !scratch) return cudaErrorInvalidValue;
-    const dim3 grid(static_cast<unsigned>(B * heads), static_cast<unsigned>(chunks));
-    decode_attn_chunk<<<grid, kThreads, 0, s>>>(static_cast<const bf16*>(qkv_dec), static_cast<const bf16*>(k_cache),
-                                                static_cast<const bf16*>(v_cache), static_cast<bf16*>(out), scratch, d,
-                                                heads, max_seq, n_keys, nullptr);
-    if (chunks > 1) {
-        const int BH = B * heads, wpb = 8;
-        decode_attn_combine<<<(BH + wpb - 1) / wpb, 32 * wpb, 0, s>>>(scratch, static_cast<bf16*>(out), d, heads,
-                                                                      chunks, BH, nullptr);
+    const size_t nf = fer_attn_decode_scratch_floats(B, heads, n_keys);
+    if (nf && !scratch) return cudaErrorInvalidValue;
+    const size_t BH = static_cast<size_t>(B) * heads;
+    int* counters = nf ? reinterpret_cast<int*>(scratch + nf - BH) : nullptr;
+    if (counters) {
+        const cudaError_t e = cudaMemsetAsync(counters, 0, BH * sizeof(int), s);
+        if (e != cudaSuccess) return e;
     }
-    return cudaGetLastError();
+    // the caches are only read on this path (d_len null)
+    return launch_decode_attn(qkv_dec, const_cast<void*>(k_cache), const_cast<void*>(v_cache), out, scratch,
+                              counters, B, d, heads, max_seq, n_keys, n_keys, nullptr, err, false, s);
 }
 
 // The same step with the position in device memory (*d_len = position of
-// the new token): K / V stored at *d_len, attention over keys 0 .. *d_len
-// (grid sized for max_seq; CTAs past the current chunk count return at
-// once), then *d_len advances by one. Launch arguments never change between
-// steps, so the sequence can be captured in a CUDA graph once and replayed.
-// scratch: fer_attn_decode_scratch_floats(B, heads, max_seq) floats.
+// the new token): attention over keys 0 .. *d_len, the new token's K / V
+// taken from qkv_dec and stored at *d_len in the same kernel (the chunk
+// count is fixed from max_seq; CTAs past the current chunk count return at
+// once). The caller advances *d_len afterwards. Launch arguments never change
+// between steps, so the sequence can be captured in a CUDA graph once and
+// replayed. scratch: fer_attn_decode_scratch_floats(B, heads, max_seq)
+// floats or more; counters: B * heads ints, zero before the first call
+// (each call leaves them zero).
 extern "C" cudaError_t fer_decode_kv_attention(const void* qkv_dec, void* k_cache, void* v_cache, void* out,
-                                               float* scratch, int B, int d, int heads, int max_seq, int* d_len,
-                                               cudaStream_t s) {
+                                               float* scratch, int* counters, int B, int d, int heads, int max_seq,
+                                               int* d_len, uint32_t* err, cudaStream_t s) {
     if (B <= 0 || d != heads * HD || max_seq <= 0 || !d_len) return cudaErrorInvalidValue;
-    const int max_chunks = (max_seq + kChunk - 1) / kChunk;
-    if (max_chunks > 1 && !scratch) return cudaErrorInvalidValue;
-    const int pieces = B * (2 * d / 8);
-    kv_store_at<<<(pieces + 255) / 256, 256, 0, s>>>(static_cast<const bf16*>(qkv_dec), static_cast<bf16*>(k_cache),
-                                                     static_cast<bf16*>(v_cache), B, d, heads, max_seq, d_len);
-    const dim3 grid(static_cast<unsigned>(B * heads), static_cast<unsigned>(max_chunks));
-    decode_attn_chunk<<<grid, kThreads, 0, s>>>(static_cast<const bf16*>(qkv_dec), static_cast<const bf16*>(k_cache),
-                                                static_cast<const bf16*>(v_cache), static_cast<bf16*>(out), scratch, d,
-                                                heads, max_seq, 0, d_len);
-    if (max_chunks > 1) {
-        const int BH = B * heads, wpb = 8;
-        decode_attn_combine<<<(BH + wpb - 1) / wpb, 32 * wpb, 0, s>>>(scratch, static_cast<bf16*>(out), d, heads,
-                                                                      max_chunks, BH, d_len);
-    }
-    return cudaGetLastError();
+    return launch_decode_attn(qkv_dec, k_cache, v_cache, out, scratch, counters, B, d, heads, max_seq, 0, max_seq,
+                              d_len, err, true, s);
 }
 
 // *d_len += v / *d_len = v on the stream.
 extern "C" cudaError_t fer_device_int_add(int* d_len, int v, cudaStream_t s) {
-    add_to_int<<<1, 1, 0, s>>>(d_len, v);
-    return cudaGetLastError();
+    const cudaError_t e = fer::host::launch_pdl(add_to_int, dim3(1), dim3(1), 0, s, d_len, v);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 extern "C" cudaError_t fer_device_int_set(int* d_len, int v, cudaStream_t s) {
     set_int<<<1, 1, 0, s>>>(d_len, v);

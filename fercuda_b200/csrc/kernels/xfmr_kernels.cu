@@ -15,6 +15,7 @@
 //                      (128 queries, head, sequence), bf16 tensor-core MMAs
 //                      (mma.sync m16n8k16) fed by ldmatrix from swizzled
 //                      shared tiles, K/V double-buffered with cp.async
+#include "pdl.cuh"
 #include "sm100_util.cuh"
 
 #include <cuda_bf16.h>
@@ -57,6 +58,7 @@ __global__ void fill_f32(float* out, size_t n, float v) {
 // One warp per token; d % 256 == 0.
 __global__ void embed_f32(const int* __restrict__ tok, const bf16* __restrict__ emb, float* __restrict__ x, int T,
                           int d, int vocab, uint32_t* err) {
+    fer::dev::pdl_begin();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
     const int id = tok[warp];
@@ -84,6 +86,7 @@ __global__ void embed_f32(const int* __restrict__ tok, const bf16* __restrict__ 
 template <int VPL>   // float4 vectors per lane = d / 128
 __global__ void ln_bf16(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
                         bf16* __restrict__ out, int T, int d, float eps) {
+    fer::dev::pdl_begin();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
     const float* row = x + static_cast<size_t>(warp) * d;
@@ -336,9 +339,10 @@ extern "C" cudaError_t fer_embed_f32(const int* tok, const void* emb, float* x, 
                                      cudaStream_t s) {
     if (d % 256) return cudaErrorInvalidValue;
     const int warps_per_block = 8;
-    embed_f32<<<(T + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(
-        tok, static_cast<const bf16*>(emb), x, T, d, vocab, err);
-    return cudaGetLastError();
+    const cudaError_t e = fer::host::launch_pdl(embed_f32, dim3((T + warps_per_block - 1) / warps_per_block),
+                                                dim3(32 * warps_per_block), 0, s, tok, static_cast<const bf16*>(emb),
+                                                x, T, d, vocab, err);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 extern "C" cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* out, int T, int d, float eps,
@@ -346,16 +350,17 @@ extern "C" cudaError_t fer_ln_bf16(const float* x, const float* g, const float* 
     const int wpb = 8;
     const dim3 grid((T + wpb - 1) / wpb), block(32 * wpb);
     bf16* o = static_cast<bf16*>(out);
+    cudaError_t e = cudaSuccess;
     switch (d / 128) {
-        case 1: if (d == 128) { ln_bf16<1><<<grid, block, 0, s>>>(x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
-        case 2: if (d == 256) { ln_bf16<2><<<grid, block, 0, s>>>(x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
-        case 4: if (d == 512) { ln_bf16<4><<<grid, block, 0, s>>>(x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
-        case 8: if (d == 1024) { ln_bf16<8><<<grid, block, 0, s>>>(x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
-        case 16: if (d == 2048) { ln_bf16<16><<<grid, block, 0, s>>>(x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
-        case 32: if (d == 4096) { ln_bf16<32><<<grid, block, 0, s>>>(x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
+        case 1: if (d == 128) { e = fer::host::launch_pdl(ln_bf16<1>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
+        case 2: if (d == 256) { e = fer::host::launch_pdl(ln_bf16<2>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
+        case 4: if (d == 512) { e = fer::host::launch_pdl(ln_bf16<4>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
+        case 8: if (d == 1024) { e = fer::host::launch_pdl(ln_bf16<8>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
+        case 16: if (d == 2048) { e = fer::host::launch_pdl(ln_bf16<16>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
+        case 32: if (d == 4096) { e = fer::host::launch_pdl(ln_bf16<32>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // Causal attention for head_dim 64; B sequences of S tokens; qkv [B*S, 3d].

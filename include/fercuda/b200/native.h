@@ -37,12 +37,18 @@ cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c, const flo
 cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N, int K, uint32_t out_dtype,
                              uint32_t* err, cudaStream_t stream);
 /* Split-K form for short M (decode steps): K split into ranges of 64-deep
- * blocks computed by separate CTAs into the f32 workspace `ws`, added in range
- * order by a second kernel that applies `epi` (for epi 3 the residual is c).
- * Deterministic; the additions are grouped differently from
- * fer_gemm_bf16_tc_ex. splits <= 0: two jobs per SM, reduced to fit ws_bytes.
- * fer_gemm_splitk_workspace_bytes: ws needed for the automatic count. */
+ * blocks computed by separate CTAs, partials added in range order before
+ * `epi` (for epi 3 the residual is c). Deterministic; the additions are
+ * grouped differently from fer_gemm_bf16_tc_ex.
+ * splits <= 0: cluster form, one cluster of fer_gemm_splitk_cluster_splits()
+ * CTAs per output tile adding the partials through distributed shared memory
+ * in one kernel (ws unused), or the single-pass kernel when that is 1.
+ * splits > 0 (or FERCUDA_SPLITK_CLUSTER=0): partials in the f32 workspace
+ * `ws`, added by a second kernel; the count is reduced to fit ws_bytes.
+ * Both forms give the same bits for the same split count.
+ * fer_gemm_splitk_workspace_bytes: ws for the workspace form's automatic count. */
 size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K);
+int fer_gemm_splitk_cluster_splits(int M, int N, int K);
 cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi, int splits,
                                     float* ws, size_t ws_bytes, uint32_t* err, cudaStream_t stream);
 /* 0 (default): 2-CTA cluster kernel for M > 128; 1: single-CTA kernel. Both
@@ -111,19 +117,22 @@ cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int S, int d, 
  * (the Q part of row b of qkv_dec [B, 3d]) against positions 0 .. n_keys-1,
  * out [B, d] bf16; split into 256-position chunks combined in chunk order,
  * scratch of fer_attn_decode_scratch_floats(B, heads, n_keys) floats (0: none
- * needed). head_dim 64. */
+ * needed). head_dim 64. err: optional device error word (bulk-copy wait
+ * timeouts). */
 cudaError_t fer_kv_store(const void* qkv, void* k_cache, void* v_cache, int B, int S, int d, int heads, int max_seq,
                          int pos0, cudaStream_t s);
 size_t fer_attn_decode_scratch_floats(int B, int heads, int n_keys);
 cudaError_t fer_attn_decode(const void* qkv_dec, const void* k_cache, const void* v_cache, void* out, float* scratch,
-                            int B, int d, int heads, int max_seq, int n_keys, cudaStream_t s);
-/* The decode step's cache store + attention with the position in device
- * memory (*d_len = position of the new token, advanced by the caller with
- * fer_device_int_add): launch arguments never change between steps, so the
- * step can be captured in a CUDA graph and replayed. scratch as
- * fer_attn_decode_scratch_floats(B, heads, max_seq). */
-cudaError_t fer_decode_kv_attention(const void* qkv_dec, void* k_cache, void* v_cache, void* out, float* scratch, int B,
-                                    int d, int heads, int max_seq, int* d_len, cudaStream_t s);
+                            int B, int d, int heads, int max_seq, int n_keys, uint32_t* err, cudaStream_t s);
+/* The decode step's cache store + attention in one kernel, with the position
+ * in device memory (*d_len = position of the new token, advanced by the
+ * caller with fer_device_int_add): launch arguments never change between
+ * steps, so the step can be captured in a CUDA graph and replayed. scratch
+ * as fer_attn_decode_scratch_floats(B, heads, max_seq); counters: B * heads
+ * ints, zero before the first call and left zero by every call. */
+cudaError_t fer_decode_kv_attention(const void* qkv_dec, void* k_cache, void* v_cache, void* out, float* scratch,
+                                    int* counters, int B, int d, int heads, int max_seq, int* d_len, uint32_t* err,
+                                    cudaStream_t s);
 cudaError_t fer_device_int_add(int* d_len, int v, cudaStream_t s);
 cudaError_t fer_device_int_set(int* d_len, int v, cudaStream_t s);
 /* Per-token layer norm, x f32 [T, d] -> out bf16, d one of 128, 256, ..., 4096. */

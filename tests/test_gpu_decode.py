@@ -156,7 +156,7 @@ def test_refused_requests(model, session):
 def test_decode_attention_kernel(B, heads, n_keys):
     """fer_attn_decode against float64 torch on random bf16 caches."""
     k = capi.kernels()
-    k.fer_attn_decode.argtypes = [C.c_void_p] * 5 + [C.c_int] * 5 + [C.c_void_p]
+    k.fer_attn_decode.argtypes = [C.c_void_p] * 5 + [C.c_int] * 5 + [C.c_void_p, C.c_void_p]
     k.fer_attn_decode.restype = C.c_int
     k.fer_attn_decode_scratch_floats.argtypes = [C.c_int] * 3
     k.fer_attn_decode_scratch_floats.restype = C.c_size_t
@@ -167,15 +167,17 @@ def test_decode_attention_kernel(B, heads, n_keys):
     vc = torch.randn(B, heads, max_seq, 64, generator=g, device="cuda").bfloat16()
     nf = k.fer_attn_decode_scratch_floats(B, heads, n_keys)
     scratch = torch.empty(max(nf, 1), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
     outs = []
     for _ in range(2):
         out = torch.full((B, d), float("nan"), device="cuda").bfloat16()
         assert k.fer_attn_decode(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(),
                                  scratch.data_ptr() if nf else None, B, d, heads, max_seq, n_keys,
-                                 torch.cuda.current_stream().cuda_stream) == 0
+                                 err.data_ptr(), torch.cuda.current_stream().cuda_stream) == 0
         torch.cuda.synchronize()
         outs.append(out)
     assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    assert int(err.item()) == 0
     q = qkv[:, :d].double().view(B, heads, 64)
     kk, vv = kc[:, :, :n_keys].double(), vc[:, :, :n_keys].double()
     p = torch.softmax(torch.einsum("bhi,bhji->bhj", q, kk) / 8.0, dim=-1)

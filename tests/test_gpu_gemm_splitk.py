@@ -28,6 +28,8 @@ def lib():
     k.fer_gemm_bf16_tc_splitk.restype = C.c_int
     k.fer_gemm_splitk_workspace_bytes.argtypes = [C.c_int] * 3
     k.fer_gemm_splitk_workspace_bytes.restype = C.c_size_t
+    k.fer_gemm_splitk_cluster_splits.argtypes = [C.c_int] * 3
+    k.fer_gemm_splitk_cluster_splits.restype = C.c_int
     return k
 
 
@@ -82,6 +84,31 @@ def test_splitk_vs_single_chain(M, N, K, epi):
     assert float(err) <= tol, float(err)
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (7, 1000, 1024), (64, 1024, 1024), (64, 3072, 1024),
+                                   (64, 4096, 1024), (64, 1024, 4096), (200, 512, 520), (128, 2048, 2048)])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_cluster_form_equals_workspace_form(M, N, K, epi):
+    k = lib()
+    S = k.fer_gemm_splitk_cluster_splits(M, N, K)
+    assert S >= 1
+    a, b, x = operands(M, N, K, seed=M + 3 * N + K)
+    got = run(k, "splitk", a, b, M, N, K, epi, x)
+    if S == 1:
+        want = run(k, "ex", a, b, M, N, K, epi, x)
+    else:
+        want = run(k, "splitk", a, b, M, N, K, epi, x, splits=S)
+    assert torch.equal(bits(got), bits(want)), S
+
+
+def test_cluster_plan_uses_large_clusters_for_decode_shapes():
+    k = lib()
+    num_k = lambda K: (K + 63) // 64
+    for N, K in [(1024, 1024), (3072, 1024), (4096, 1024), (1024, 4096)]:
+        S = k.fer_gemm_splitk_cluster_splits(64, N, K)
+        assert 2 <= S <= min(16, num_k(K)), (N, K, S)
+    assert k.fer_gemm_splitk_cluster_splits(64, 32000, 1024) == 1     # 125 tiles: no split
+
+
 def test_splits_shrink_to_the_workspace():
     k = lib()
     M, N, K = 64, 2048, 4096
@@ -93,5 +120,6 @@ def test_splits_shrink_to_the_workspace():
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     c = torch.empty(M, N, device="cuda")
     ws = torch.empty(16, device="cuda")
-    assert k.fer_gemm_bf16_tc_splitk(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, 0, 0, ws.data_ptr(), 64,
+    # the workspace form (explicit count) refuses a workspace too small for one split
+    assert k.fer_gemm_bf16_tc_splitk(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, 0, 5, ws.data_ptr(), 64,
                                      err.data_ptr(), torch.cuda.current_stream().cuda_stream) != 0
