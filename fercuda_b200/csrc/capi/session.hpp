@@ -149,7 +149,7 @@ cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, cons
 cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s);
 size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K);
 cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi, int splits,
-                                    float* ws, size_t ws_bytes, uint32_t* err, cudaStream_t stream);
+                                    float* ws, size_t ws_bytes, int flags, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_kv_store(const void* qkv, void* k_cache, void* v_cache, int B, int S, int d, int heads, int max_seq,
                          int pos0, cudaStream_t s);
 size_t fer_attn_decode_scratch_floats(int B, int heads, int n_keys);

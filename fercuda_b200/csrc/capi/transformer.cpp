@@ -557,7 +557,7 @@ fer_status_t fer_transformer_decode(fer_session_t* session, uint64_t model, uint
     // the device and every buffer address is fixed, so the whole step is
     // captured once per batch size and replayed (first call eager).
     auto gemm = [&](const void* a, const void* b, void* cc, int N, int K, int epi) {
-        return fer_gemm_bf16_tc_splitk(a, b, cc, B, N, K, epi, 0, kc.gemm_ws, kc.gemm_ws_bytes, err, st);
+        return fer_gemm_bf16_tc_splitk(a, b, cc, B, N, K, epi, 0, kc.gemm_ws, kc.gemm_ws_bytes, 1, err, st);
     };
     cudaError_t e = cudaSuccess;
     auto issue = [&]() {

@@ -274,7 +274,7 @@ template <bool kCluster>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, int splits, int kps,
-                        void* __restrict__ out, uint32_t* err) {
+                        void* __restrict__ out, int b_static, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -320,14 +320,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = bars.tmem_base;
     // Setup above touches no global memory; under programmatic launch it
-    // overlaps the previous kernel.
-    fer::dev::pdl_begin();
+    // overlaps the previous kernel. The producer waits below, after it has
+    // fetched what does not depend on that kernel.
+    if (warp != 0) fer::dev::pdl_begin();
 
     volatile int* abort_flag = &bars.abort_flag;
     // Each role loop is run by its whole warp (waits voted across the warp,
     // issue from lane 0) so every warp reaches the final barrier converged.
     if (warp == 0) {
         // ---------------- TMA producer
+        auto load_b = [&](int s, int nb, int kblock) {
+            uint8_t* sb = smem + s * STAGE_BYTES + A_BYTES;
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+                tma_load_2d(sb + c * (BK * 128), &tmB, nb * BN + c * 64, kblock * BK, &bars.full[s]);
+        };
+        // b_static: B (weights) is not written by the previous kernel, so
+        // the first job's first STAGES B tiles are fetched before the wait.
+        int pre = 0;
+        if (b_static && static_cast<int>(blockIdx.x) < num_jobs) {
+            int mb, nb, kb0, nk;
+            tile_coords(job_tile(blockIdx.x), num_m, num_n, &mb, &nb);
+            job_k(blockIdx.x, &kb0, &nk);
+            pre = nk < STAGES ? nk : STAGES;
+            if (lane == 0)
+                for (int kt = 0; kt < pre; ++kt) {
+                    mbar_arrive_expect_tx(&bars.full[kt], STAGE_BYTES);
+                    load_b(kt, nb, kb0 + kt);
+                }
+            __syncwarp();
+        }
+        fer::dev::pdl_begin();
         int it = 0;
         for (int t = blockIdx.x; t < num_jobs && !warp_flag(abort_flag); t += gridDim.x) {
             int mb, nb, kb0, nk;
@@ -336,19 +359,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kt = 0; kt < nk; ++kt, ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+                if (it < pre) {
+                    // slot armed and its B in flight since before the wait
+                    if (lane == 0) tma_load_2d(smem + s * STAGE_BYTES, &tmA, (kb0 + kt) * BK, mb * BM, &bars.full[s]);
+                    __syncwarp();
+                    continue;
+                }
                 if (!__all_sync(0xffffffffu, mbar_wait(&bars.empty[s], ph ^ 1u))) {
                     if (lane == 0) report(err, kErrTimeoutSync);
                     *abort_flag = 1;
                     break;
                 }
                 if (lane == 0) {
-                    uint8_t* sa = smem + s * STAGE_BYTES;
-                    uint8_t* sb = sa + A_BYTES;
                     mbar_arrive_expect_tx(&bars.full[s], STAGE_BYTES);
-                    tma_load_2d(sa, &tmA, (kb0 + kt) * BK, mb * BM, &bars.full[s]);
-#pragma unroll
-                    for (int c = 0; c < BN / 64; ++c)
-                        tma_load_2d(sb + c * (BK * 128), &tmB, nb * BN + c * 64, (kb0 + kt) * BK, &bars.full[s]);
+                    tma_load_2d(smem + s * STAGE_BYTES, &tmA, (kb0 + kt) * BK, mb * BM, &bars.full[s]);
+                    load_b(s, nb, kb0 + kt);
                 }
                 __syncwarp();
             }
@@ -879,8 +904,10 @@ extern "C" int fer_gemm_tc_clusters() { return g_gemm_clusters; }
 // other resid is first copied into c (it must not partly overlap c).
 // Requires K % 8 == 0 and N % 8 == 0 (16-byte row pitches for the tensor
 // maps) and 16-byte aligned operands; returns cudaErrorInvalidValue otherwise.
-extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c, const float* resid, int M, int N,
-                                           int K, int epi, uint32_t* err, cudaStream_t stream) {
+namespace {
+
+cudaError_t gemm_ex(const void* a, const void* b, void* c, const float* resid, int M, int N, int K, int epi,
+                    int b_static, uint32_t* err, cudaStream_t stream) {
     if (M <= 0 || N <= 0 || K <= 0 || (K % 8) || (N % 8)) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 15u)
         return cudaErrorInvalidValue;
@@ -935,8 +962,15 @@ extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c
     const int grid = tiles < sm_count() ? tiles : sm_count();
     const cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES,
                                                 stream, ma, mb, mc, M, N, K, epi, 1, (K + BK - 1) / BK,
-                                                static_cast<void*>(nullptr), err);
+                                                static_cast<void*>(nullptr), b_static, err);
     return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" cudaError_t fer_gemm_bf16_tc_ex(const void* a, const void* b, void* c, const float* resid, int M, int N,
+                                           int K, int epi, uint32_t* err, cudaStream_t stream) {
+    return gemm_ex(a, b, c, resid, M, N, K, epi, 0, err, stream);
 }
 
 namespace {
@@ -1096,9 +1130,13 @@ extern "C" int fer_gemm_splitk_cluster_splits(int M, int N, int K) {
 // partials fit ws_bytes (cudaErrorInvalidValue if one split does not), and
 // with the cluster form off, splits <= 0 gives every SM one job. Both forms
 // give the same bits for the same split count.
+// flags bit 0: b is not written by the kernel just before this call on the
+// stream (weights), so its first tiles are fetched before the programmatic
+// launch wait, overlapping that kernel's tail.
 extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi,
-                                               int splits, float* ws, size_t ws_bytes, uint32_t* err,
+                                               int splits, float* ws, size_t ws_bytes, int flags, uint32_t* err,
                                                cudaStream_t stream) {
+    const int b_static = flags & 1;
     if (M <= 0 || N <= 0 || K <= 0 || (K % 8) || (N % 8) || epi < kEpiF32 || epi > kEpiResidF32 || !ws)
         return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c) |
@@ -1107,8 +1145,8 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
     int kps = 0;
     if (splits <= 0) {
         const int cs = csplit_plan(M, N, K, &kps);
-        if (cs == 1) return fer_gemm_bf16_tc_ex(a, b, c, epi == kEpiResidF32 ? static_cast<const float*>(c) : nullptr,
-                                                M, N, K, epi, err, stream);
+        if (cs == 1) return gemm_ex(a, b, c, epi == kEpiResidF32 ? static_cast<const float*>(c) : nullptr, M, N, K,
+                                    epi, b_static, err, stream);
         if (cs >= 2) {
             CUtensorMap ma, mb;
             if (!make_map(&ma, a, static_cast<uint64_t>(M), static_cast<uint64_t>(K), BM) ||
@@ -1131,7 +1169,7 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
             cfg.numAttrs = fer::host::pdl_enabled() ? 2 : 1;
             // the C map is not used by the cluster form
             const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<true>, ma, mb, ma, M, N, K, epi, cs,
-                                                     kps, c, err);
+                                                     kps, c, b_static, err);
             return e != cudaSuccess ? e : cudaGetLastError();
         }
     }
@@ -1157,7 +1195,7 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
     const int grid = jobs < sm_count() ? jobs : sm_count();
     cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES, stream,
                                           ma, mb, mc, M, N, K, static_cast<int>(kEpiF32), splits, kps,
-                                          static_cast<void*>(nullptr), err);
+                                          static_cast<void*>(nullptr), b_static, err);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const size_t total4 = static_cast<size_t>(M) * N / 4;

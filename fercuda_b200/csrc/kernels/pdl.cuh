@@ -8,6 +8,12 @@
 // visible; launch_dependents then lets the next kernel be scheduled. Without
 // a programmatic predecessor both are no-ops, so the kernels stay correct
 // under plain launches. FERCUDA_PDL=0 launches without the attribute.
+//
+// Since every kernel of a chain triggers only after its own wait, a kernel
+// that starts running finds the kernel two places back (and all before it)
+// complete. Data that the immediately preceding kernel does not write
+// (weights, cache rows of earlier steps) may therefore be read before
+// pdl_wait(); everything else after it.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -17,9 +23,12 @@
 
 namespace fer::dev {
 
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 __device__ __forceinline__ void pdl_begin() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;");
+    pdl_wait();
+    pdl_trigger();
 }
 
 }  // namespace fer::dev

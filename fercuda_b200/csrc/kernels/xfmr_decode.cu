@@ -121,7 +121,12 @@ __global__ void __launch_bounds__(kThreads) decode_attn(const __grid_constant__ 
                                                         int heads, int max_seq, int n_keys_arg,
                                                         const int* __restrict__ d_len, uint32_t* err) {
     using namespace fer::dev;
-    pdl_begin();
+    // A decode step (d_len given) finds *d_len and the cache rows below it
+    // written two or more kernels back, so it reads them (and issues the
+    // first stage loads) before the programmatic launch wait; q and the new
+    // row come from the kernel just before and are read after it.
+    const bool early = d_len != nullptr;
+    if (!early) pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full[kStages];
     __shared__ int is_last;
@@ -155,6 +160,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn(const __grid_constant__ 
     };
     if (t == 0)
         for (int i = 0; i < kStages && i < nsub; ++i) issue(i);
+    if (early) pdl_wait();
+    pdl_trigger();
 
     const bf16* qrow = qkv_dec + static_cast<size_t>(b) * 3 * d;
     float qr[16];

@@ -46,11 +46,14 @@ cudaError_t fer_gemm_bf16_tc(const void* a, const void* b, void* c, int M, int N
  * splits > 0 (or FERCUDA_SPLITK_CLUSTER=0): partials in the f32 workspace
  * `ws`, added by a second kernel; the count is reduced to fit ws_bytes.
  * Both forms give the same bits for the same split count.
+ * flags bit 0: b is not written by the kernel just before this call on the
+ * stream (weights); its first tiles are then fetched before the programmatic
+ * launch wait, overlapping that kernel.
  * fer_gemm_splitk_workspace_bytes: ws for the workspace form's automatic count. */
 size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K);
 int fer_gemm_splitk_cluster_splits(int M, int N, int K);
 cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi, int splits,
-                                    float* ws, size_t ws_bytes, uint32_t* err, cudaStream_t stream);
+                                    float* ws, size_t ws_bytes, int flags, uint32_t* err, cudaStream_t stream);
 /* 0 (default): 2-CTA cluster kernel for M > 128; 1: single-CTA kernel. Both
  * give the same bits. Process-wide. */
 void fer_gemm_tc_set_mode(int mode);

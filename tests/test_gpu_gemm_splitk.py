@@ -24,7 +24,7 @@ def lib():
     k = capi.kernels()
     k.fer_gemm_bf16_tc_ex.argtypes = [P, P, P, P] + [C.c_int] * 4 + [P, P]
     k.fer_gemm_bf16_tc_ex.restype = C.c_int
-    k.fer_gemm_bf16_tc_splitk.argtypes = [P, P, P] + [C.c_int] * 5 + [P, C.c_size_t, P, P]
+    k.fer_gemm_bf16_tc_splitk.argtypes = [P, P, P] + [C.c_int] * 5 + [P, C.c_size_t, C.c_int, P, P]
     k.fer_gemm_bf16_tc_splitk.restype = C.c_int
     k.fer_gemm_splitk_workspace_bytes.argtypes = [C.c_int] * 3
     k.fer_gemm_splitk_workspace_bytes.restype = C.c_size_t
@@ -41,7 +41,7 @@ def operands(M, N, K, seed):
     return a, b, x
 
 
-def run(k, fn, a, b, M, N, K, epi, x, splits=0, ws_bytes=None):
+def run(k, fn, a, b, M, N, K, epi, x, splits=0, ws_bytes=None, flags=0):
     f32 = epi in (0, 3)
     c = x.clone() if epi == 3 else torch.full((M, N), float("nan"), device="cuda",
                                              dtype=torch.float32 if f32 else torch.bfloat16)
@@ -56,7 +56,7 @@ def run(k, fn, a, b, M, N, K, epi, x, splits=0, ws_bytes=None):
             nbytes = max(nbytes, splits * ((M + 127) // 128) * 128 * N * 4)
         ws = torch.empty(max(nbytes // 4, 4), device="cuda")
         rc = k.fer_gemm_bf16_tc_splitk(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, epi, splits,
-                                       ws.data_ptr(), nbytes, err.data_ptr(), st)
+                                       ws.data_ptr(), nbytes, flags, err.data_ptr(), st)
     assert rc == 0
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -79,6 +79,8 @@ def test_splitk_vs_single_chain(M, N, K, epi):
     assert torch.equal(bits(got), bits(again))
     one = run(k, "splitk", a, b, M, N, K, epi, x, splits=1)
     assert torch.equal(bits(one), bits(want))
+    # static weights (B fetched before the launch wait): same bits
+    assert torch.equal(bits(run(k, "splitk", a, b, M, N, K, epi, x, flags=1)), bits(got))
     tol = 1e-5 if epi in (0, 3) else 4e-3
     err = (got.float() - want.float()).abs().max() / want.float().abs().max()
     assert float(err) <= tol, float(err)
@@ -121,5 +123,5 @@ def test_splits_shrink_to_the_workspace():
     c = torch.empty(M, N, device="cuda")
     ws = torch.empty(16, device="cuda")
     # the workspace form (explicit count) refuses a workspace too small for one split
-    assert k.fer_gemm_bf16_tc_splitk(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, 0, 5, ws.data_ptr(), 64,
+    assert k.fer_gemm_bf16_tc_splitk(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, 0, 5, ws.data_ptr(), 64, 0,
                                      err.data_ptr(), torch.cuda.current_stream().cuda_stream) != 0
