@@ -139,15 +139,74 @@ enum : int { kEpiF32 = 0, kEpiBF16 = 1, kEpiGeluBF16 = 2, kEpiResidF32 = 3 };
 // so with s = 1 - erf(|x| / sqrt 2): 1 + erf(x / sqrt 2) = s for x < 0 (no
 // cancellation) and 2 - s otherwise. Max error against the exact function is
 // ~4e-7 absolute, far below the bf16 rounding of the result.
+// Every step is an explicitly rounded operation (no contraction), so the
+// scalar form and the paired form below give the same bits.
 __device__ __forceinline__ float gelu_erf(float x) {
-    const float z = fabsf(x) * 0.70710678118654752f;
+    const float z = __fmul_rn(fabsf(x), 0.70710678118654752f);
     float t, e;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.0f)));
-    const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f),
-                                0.254829592f);
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-z * z * 1.4426950408889634f));
-    const float s = poly * e;
-    return 0.5f * x * (x < 0.0f ? s : 2.0f - s);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmaf_rn(0.3275911f, z, 1.0f)));
+    float h = __fmaf_rn(t, 1.061405429f, -1.453152027f);
+    h = __fmaf_rn(t, h, 1.421413741f);
+    h = __fmaf_rn(t, h, -0.284496736f);
+    h = __fmaf_rn(t, h, 0.254829592f);
+    const float poly = __fmul_rn(t, h);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(__fmul_rn(z, z), -1.4426950408889634f)));
+    const float s = __fmul_rn(poly, e);
+    return __fmul_rn(__fmul_rn(0.5f, x), x < 0.0f ? s : __fsub_rn(2.0f, s));
+}
+
+// Two lanes of f32x2 (packed, one instruction per pair on sm_100).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_splat(float v) { return f2_pack(v, v); }
+
+// gelu_erf of a pair, the same operations on packed f32x2 (bit-identical
+// to two scalar calls; about half the instructions in the epilogue).
+__device__ __forceinline__ void gelu_erf2(float& x0, float& x1) {
+    const uint64_t x = f2_pack(x0, x1);
+    const uint64_t z = f2_mul(x & 0x7fffffff7fffffffull, f2_splat(0.70710678118654752f));
+    float d0, d1, t0, t1;
+    f2_unpack(f2_fma(f2_splat(0.3275911f), z, f2_splat(1.0f)), d0, d1);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(d0));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(d1));
+    const uint64_t t = f2_pack(t0, t1);
+    uint64_t h = f2_fma(t, f2_splat(1.061405429f), f2_splat(-1.453152027f));
+    h = f2_fma(t, h, f2_splat(1.421413741f));
+    h = f2_fma(t, h, f2_splat(-0.284496736f));
+    h = f2_fma(t, h, f2_splat(0.254829592f));
+    const uint64_t poly = f2_mul(t, h);
+    float a0, a1, e0, e1;
+    f2_unpack(f2_mul(f2_mul(z, z), f2_splat(-1.4426950408889634f)), a0, a1);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
+    const uint64_t s = f2_mul(poly, f2_pack(e0, e1));
+    const uint64_t q = f2_sub(f2_splat(2.0f), s);
+    float s0, s1, q0, q1;
+    f2_unpack(s, s0, s1);
+    f2_unpack(q, q0, q1);
+    const uint64_t r = f2_pack(x0 < 0.0f ? s0 : q0, x1 < 0.0f ? s1 : q1);
+    f2_unpack(f2_mul(f2_mul(f2_splat(0.5f), x), r), x0, x1);
 }
 
 // bf16 pair {lo, hi} (round to nearest even), lo in the low half.
@@ -488,10 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             float a0 = __uint_as_float(r[2 * j]), a1 = __uint_as_float(r[2 * j + 1]);
-                            if (gelu) {
-                                a0 = gelu_erf(a0);
-                                a1 = gelu_erf(a1);
-                            }
+                            if (gelu) gelu_erf2(a0, a1);
                             w[16 * h2 + j] = pack_bf16x2(a0, a1);
                         }
                     }
@@ -778,10 +834,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
                             float a0 = __uint_as_float(r[2 * j]), a1 = __uint_as_float(r[2 * j + 1]);
-                            if (gelu) {
-                                a0 = gelu_erf(a0);
-                                a1 = gelu_erf(a1);
-                            }
+                            if (gelu) gelu_erf2(a0, a1);
                             w[16 * h2 + j] = pack_bf16x2(a0, a1);
                         }
                     }
