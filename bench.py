@@ -15,6 +15,8 @@ default run on one GPU:
   gemm               bf16 8192^3 -> f32, deterministic tcgen05 GEMM       TFLOP/s
   tlsf               1M-op alloc/free trace (256 B - 16 MiB, 60/40, live <= 64 GiB),
                      each allocation filled by a kernel; alloc latency   ns (p50)
+  decode             KV-cache decoding on the benchmark model, 64 sequences
+                     after a 512-token prompt, one token each per step   tokens/s
 
 Timing: CUDA events on the session stream over exactly K steps after W
 warm-up steps, barrier + synchronize on both sides, max over ranks.
@@ -581,8 +583,14 @@ class Tlsf:
         return out
 
 
+class Decode:
+    """Incremental decoding (fer_transformer_decode), run by decode_steps."""
+    metric = "decode tokens/s (one token per sequence per step)"
+    unit = "tokens/s"
+
+
 WORKLOADS = {"transformer": Transformer, "softmax_layernorm": Rows, "fused_elementwise": Chain, "gemm": Gemm,
-             "tlsf": Tlsf}
+             "tlsf": Tlsf, "decode": Decode}
 
 
 # ================================================================ runners
@@ -667,14 +675,14 @@ def decode_steps(s, capi, synth, torch, batch=64, prompt=512, steps=32):
     L, d, h, F, V = c["layers"], c["d_model"], c["heads"], c["ffn"], c["vocab"]
     m = capi.Transformer(s, L, d, h, F, V, batch * prompt, c["eps"])
     m.init_weights(c["weight_seed"], 0.02)
-    u = synth.uniform01(c["token_seed"], batch * (prompt + steps + 4))
-    toks = np.minimum((u * V).astype(np.int32), V - 1).reshape(batch, prompt + steps + 4)
-    cache = m.kv_create(batch, prompt + steps + 4)
+    u = synth.uniform01(c["token_seed"], batch * (prompt + steps + 5))
+    toks = np.minimum((u * V).astype(np.int32), V - 1).reshape(batch, prompt + steps + 5)
+    cache = m.kv_create(batch, prompt + steps + 5)
     bt = s.alloc(capi.FER_DTYPE_I32, [batch, prompt])
     s.upload(bt, np.ascontiguousarray(toks[:, :prompt]))
     bl = s.alloc(capi.FER_DTYPE_F32, [batch, V])
     dts = []
-    for k in range(steps + 4):
+    for k in range(steps + 5):
         b = s.alloc(capi.FER_DTYPE_I32, [batch])
         s.upload(b, np.ascontiguousarray(toks[:, prompt + k]))
         dts.append(b)
@@ -696,6 +704,12 @@ def decode_steps(s, capi, synth, torch, batch=64, prompt=512, steps=32):
     e1.record(ext)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
+    # one more step inside a profiler range (a no-op unless a profiler with
+    # --profile-from-start off is attached): the launch list of one step
+    torch.cuda.profiler.start()
+    m.decode(cache, dts[4 + steps], bl)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     errs = s.device_errors()
     ctx = prompt + 4 + steps / 2                 # mean keys per step
     kv_bytes = L * batch * d * 2 * 2 * (ctx + 1)   # K and V read (bf16) plus the new row
@@ -760,6 +774,10 @@ def run_reference(args, rank):
                 "e2e": {"value": v, "unit": "ns", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         emit(line)
+        return
+    if cls is Decode:
+        emit({"impl": "reference", "unavailable": "the reference has no KV-cache decoding path to time "
+                                                  "(its transformer is a full forward only)"})
         return
     vals = []
     for _ in range(args.warmup if cls is not Transformer else 1):
@@ -831,6 +849,27 @@ def main():
         pool = max(pool, 2 * (2 * nbuf * 4 * args.elements) + (1 << 30))
     s = capi.Session(local, pool_bytes=pool)
     stream = torch.cuda.ExternalStream(s.stream())
+
+    if cls is Decode:
+        if rank == 0:
+            clocks = ClockSampler(local)
+            clocks.start()
+            time.sleep(0.25)
+            clocks.mark(True)
+            r = decode_steps(s, capi, synth, torch, steps=args.steps)
+            clocks.mark(False)
+            line = {"metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": 1, "steps": args.steps,
+                    "warmup": 4, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                    "config": {"workload": "decode_L8_d1024_h16_F4096_V32000_B64_prompt512",
+                               "batch": r["batch"], "prompt": r["prompt"]},
+                    "roofline": r["roofline"], "prefill_ms": r["prefill_ms"], "clocks": clocks.stop(),
+                    "device_error_bits": r["device_error_bits"], "api": r["api"]}
+            emit(line)
+        s.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     if cls is Tlsf:
         if rank == 0:
