@@ -4,18 +4,19 @@
 // qkv: [B*S, 3*d] bf16 row-major (q | k | v; head h at columns h*64 of each
 // third); out: [B*S, d] bf16. S must be a multiple of 128.
 //
-// One CTA per (128-query tile, head, sequence), two CTAs per SM. Per key
-// block j (128 keys, j = 0 .. query tile):
-//   warp 0      TMA: Q once, K_j into a 2-deep ring, V_j into one buffer,
-//               all 128-byte swizzled [128 rows x 64 bf16] boxes
-//   warp 1      tcgen05.mma from one thread: S = Q K_j^T (M128 N128, f32 in
+// One CTA per (128-query tile, head, sequence), three CTAs per SM (64 KB of
+// shared memory and 128 tensor-memory columns each). Per key block j (64
+// keys, j = 0 .. 2 * query tile + 1):
+//   warp 0      TMA: Q once ([128 rows x 64 bf16]), K_j and V_j into 2-deep
+//               rings ([64 rows x 64 bf16]), all 128-byte swizzled boxes
+//   warp 1      tcgen05.mma from one thread: S = Q K_j^T (M128 N64, f32 in
 //               tensor memory), issued for block j+1 as soon as the softmax
 //               threads have read block j's scores, then O += P_j V_j (M128
-//               N64, K = 128 keys) once P_j is written
+//               N64, K = 64 keys) once P_j is written
 //   warps 2..5  one query row per thread: scores from tensor memory
-//               (tcgen05.ld), causal mask on the diagonal block, running max
-//               in the log2 domain, p = 2^(s*scale - m) (ex2.approx), row sum
-//               in f32, P rounded to bf16 into swizzled shared memory (the
+//               (tcgen05.ld), causal mask on the two diagonal blocks, running
+//               max in the log2 domain, p = 2^(s*scale - m) (ex2.approx), row
+//               sum in f32, P rounded to bf16 into swizzled shared memory (the
 //               A operand of the P.V MMA). O accumulates in tensor memory
 //               across key blocks; when a row's max grows the softmax thread
 //               rescales its O row in place (tcgen05.ld / st) before the
@@ -38,20 +39,24 @@ namespace {
 using namespace fer::dev;
 
 constexpr int TQ = 128;                   // queries per CTA
-constexpr int TK = 128;                   // keys per block
-constexpr int TILE_BYTES = 128 * 128;     // [128 rows x 64 bf16], 16 KiB
+constexpr int TK = 64;                    // keys per block
+constexpr int Q_BYTES = TQ * 128;         // [128 rows x 64 bf16], 16 KiB
+constexpr int KV_BYTES = TK * 128;        // [64 rows x 64 bf16], 8 KiB
+constexpr int P_BYTES = TQ * TK * 2;      // [128 rows x 64 keys bf16], 16 KiB
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = TILE_BYTES;         // two K buffers
-constexpr int OFF_V = 3 * TILE_BYTES;
-constexpr int OFF_P = 4 * TILE_BYTES;     // P: keys 0..63 at +0, keys 64..127 at +16 KiB
-constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024;
+constexpr int OFF_K = Q_BYTES;            // two K buffers
+constexpr int OFF_V = OFF_K + 2 * KV_BYTES;   // two V buffers
+constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
+constexpr int SMEM_BYTES = OFF_P + P_BYTES + 1024;
 constexpr int kThreads = 192;
-constexpr uint32_t TMEM_COLS = 256;       // S at columns [0, 128), O at [128, 192)
-constexpr uint32_t COL_O = 128;
+constexpr int kCtasPerSm = 3;
+constexpr uint32_t TMEM_COLS = 128;       // S at columns [0, 64), O at [64, 128)
+constexpr uint32_t COL_O = 64;
+static_assert(kCtasPerSm * TMEM_COLS <= 512, "tensor memory per SM");
 
 // kind::f16 instruction descriptors: f32 accumulate, bf16 A and B, M = 128.
-// S = Q K^T: A and B K-major, N = 128. O = P V: A K-major, B (V) N-major, N = 64.
-constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+// S = Q K^T: A and B K-major, N = 64. O = P V: A K-major, B (V) N-major, N = 64.
+constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint32_t kIdescPV =
     (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
 
@@ -59,8 +64,8 @@ struct Bars {
     uint64_t q_full;
     uint64_t k_full[2];
     uint64_t k_empty[2];
-    uint64_t v_full;
-    uint64_t v_empty;
+    uint64_t v_full[2];
+    uint64_t v_empty[2];
     uint64_t s_full;
     uint64_t s_free;
     uint64_t p_full;
@@ -165,9 +170,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
-    attn_causal_tc(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out, int S, int d,
-                   float scale_log2, uint32_t* err) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+    attn_causal_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
+                   __nv_bfloat16* __restrict__ out, int S, int d, float scale_log2, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -176,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);   // longest tiles first
     const int h = blockIdx.y;
     const int seq_row0 = static_cast<int>(blockIdx.z) * S;
-    const int n_k = qt + 1;                                                             // key blocks 0 .. qt
+    const int n_k = (qt + 1) * (TQ / TK);                                               // keys 0 .. end of tile
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -184,9 +189,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars.k_full[i], 1);
             mbar_init(&bars.k_empty[i], 1);
+            mbar_init(&bars.v_full[i], 1);
+            mbar_init(&bars.v_empty[i], 1);
         }
-        mbar_init(&bars.v_full, 1);
-        mbar_init(&bars.v_empty, 1);
         mbar_init(&bars.s_full, 1);
         mbar_init(&bars.s_free, 4);
         mbar_init(&bars.p_full, 4);
@@ -210,8 +215,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 0) {
         // ---------------- TMA producer
         if (lane == 0) {
-            mbar_arrive_expect_tx(&bars.q_full, TILE_BYTES);
-            tma_load_2d(sbase + OFF_Q, &tm, h * 64, seq_row0 + qt * TQ, &bars.q_full);
+            mbar_arrive_expect_tx(&bars.q_full, Q_BYTES);
+            tma_load_2d(sbase + OFF_Q, &tmq, h * 64, seq_row0 + qt * TQ, &bars.q_full);
         }
         __syncwarp();
         for (int j = 0; j < n_k && !warp_flag(abort_flag); ++j) {
@@ -223,18 +228,19 @@ __global__ void __launch_bounds__(kThreads, 2)
                 break;
             }
             if (lane == 0) {
-                mbar_arrive_expect_tx(&bars.k_full[st], TILE_BYTES);
-                tma_load_2d(sbase + OFF_K + st * TILE_BYTES, &tm, d + h * 64, seq_row0 + j * TK, &bars.k_full[st]);
+                mbar_arrive_expect_tx(&bars.k_full[st], KV_BYTES);
+                tma_load_2d(sbase + OFF_K + st * KV_BYTES, &tmkv, d + h * 64, seq_row0 + j * TK, &bars.k_full[st]);
             }
             __syncwarp();
-            if (!warp_wait(&bars.v_empty, (static_cast<uint32_t>(j) & 1u) ^ 1u)) {
+            if (!warp_wait(&bars.v_empty[st], (use & 1u) ^ 1u)) {
                 if (lane == 0) report(err, kErrTimeoutSync);
                 *abort_flag = 1;
                 break;
             }
             if (lane == 0) {
-                mbar_arrive_expect_tx(&bars.v_full, TILE_BYTES);
-                tma_load_2d(sbase + OFF_V, &tm, 2 * d + h * 64, seq_row0 + j * TK, &bars.v_full);
+                mbar_arrive_expect_tx(&bars.v_full[st], KV_BYTES);
+                tma_load_2d(sbase + OFF_V + st * KV_BYTES, &tmkv, 2 * d + h * 64, seq_row0 + j * TK,
+                            &bars.v_full[st]);
             }
             __syncwarp();
         }
@@ -248,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (j > 0 && !warp_wait(&bars.s_free, static_cast<uint32_t>(j - 1) & 1u)) return false;
             fence_after();
             if (lane == 0) {
-                const uint32_t q = sbase + OFF_Q, k = sbase + OFF_K + st * TILE_BYTES;
+                const uint32_t q = sbase + OFF_Q, k = sbase + OFF_K + st * KV_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     mma(tmem, sdesc(q + kk * 32, 16, 1024), sdesc(k + kk * 32, 16, 1024), kIdescS, kk ? 1u : 0u);
@@ -262,16 +268,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int j = 0; j < n_k && ok && !warp_flag(abort_flag); ++j) {
             const uint32_t ph = static_cast<uint32_t>(j) & 1u;
             if (j + 1 < n_k && !(ok = issue_s(j + 1))) break;
-            ok = warp_wait(&bars.p_full, ph) && warp_wait(&bars.v_full, ph);
+            const int st = j & 1;
+            ok = warp_wait(&bars.p_full, ph) && warp_wait(&bars.v_full[st], static_cast<uint32_t>(j >> 1) & 1u);
             if (!ok) break;
             fence_after();
             if (lane == 0) {
-                const uint32_t p = sbase + OFF_P, v = sbase + OFF_V;
+                const uint32_t p = sbase + OFF_P, v = sbase + OFF_V + st * KV_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma(tmem + COL_O, sdesc(p + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024),
-                        sdesc(v + kk * 2048, TILE_BYTES, 1024), kIdescPV, (j | kk) ? 1u : 0u);
-                commit(&bars.v_empty);
+                for (int kk = 0; kk < TK / 16; ++kk)
+                    mma(tmem + COL_O, sdesc(p + kk * 32, 16, 1024), sdesc(v + kk * 2048, KV_BYTES, 1024), kIdescPV,
+                        (j | kk) ? 1u : 0u);
+                commit(&bars.v_empty[st]);
                 commit(&bars.o_full);
             }
             __syncwarp();
@@ -294,22 +301,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                 break;
             }
             fence_after();
-            float sv[128];
+            float sv[TK];
             tmem_ld64(trow, sv);
-            tmem_ld64(trow + 64, sv + 64);
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars.s_free);   // S_{j+1} may overwrite S now
-            if (j == qt) {
+            const int kb = j * TK - qt * TQ;            // first key of the block, relative to the tile's first query
+            if (kb + TK - 1 > 0) {
 #pragma unroll
-                for (int e = 0; e < 128; ++e)
-                    if (e > r) sv[e] = -INFINITY;               // causal mask on the diagonal block
+                for (int e = 0; e < TK; ++e)
+                    if (kb + e > r) sv[e] = -INFINITY;          // causal mask on the diagonal blocks
             }
             float mx[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) mx[e] = sv[e];
 #pragma unroll
-            for (int e = 8; e < 128; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[e]);
+            for (int e = 8; e < TK; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[e]);
             const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             const float m_new = fmaxf(m, smax * scale_log2);
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int e = 0; e < 8; ++e) sm[e] = 0.0f;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < TK / 32; ++c) {
                 uint32_t w[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
@@ -336,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     sm[(e + 1) & 7] += p1;
                     w[e >> 1] = pack_bf16x2(p0, p1);
                 }
-                const uint32_t prow = sbase + OFF_P + (c >> 1) * TILE_BYTES + r * 128;
+                const uint32_t prow = sbase + OFF_P + r * 128;
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4) {
                     const int chunk = (c & 1) * 4 + q4;
@@ -421,12 +428,16 @@ extern "C" cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int
     if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(out)) & 15u) return cudaErrorNotSupported;
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
-    CUtensorMap tm;
+    // two maps over qkv [B*S, 3d]: Q boxes of 128 rows, K / V boxes of 64
+    CUtensorMap tmq, tmkv;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(3) * d, static_cast<cuuint64_t>(B) * S};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(3) * d * 2};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t boxq[2] = {64, TQ}, boxkv[2] = {64, TK};
     const cuuint32_t estr[2] = {1, 1};
-    if (fn(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, box, estr,
+    if (fn(&tmq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxq, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        fn(&tmkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxkv, estr,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorNotSupported;
@@ -438,7 +449,7 @@ extern "C" cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int
     }
     const float scale_log2 = 1.4426950408889634f / 8.0f;   // log2(e) / sqrt(64)
     const dim3 grid(S / TQ, heads, B);
-    attn_causal_tc<<<grid, kThreads, SMEM_BYTES, stream>>>(tm, static_cast<__nv_bfloat16*>(out), S, d, scale_log2,
-                                                           err);
+    attn_causal_tc<<<grid, kThreads, SMEM_BYTES, stream>>>(tmq, tmkv, static_cast<__nv_bfloat16*>(out), S, d,
+                                                           scale_log2, err);
     return cudaGetLastError();
 }
