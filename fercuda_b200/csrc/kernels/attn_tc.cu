@@ -27,6 +27,7 @@
 // Every wait is bounded (about one second): on timeout the kernel records an
 // error bit, stops, releases tensor memory and returns. No TMA multicast.
 #include "sm100_util.cuh"
+#include "tmap.cuh"
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -401,22 +402,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+using fer::host::EncodeTiledFn;
 
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
+EncodeTiledFn encode_fn() { return fer::host::encode_tiled_fn(); }
 
 }  // namespace
 

@@ -32,6 +32,7 @@
 // No TMA multicast is used anywhere.
 #include "pdl.cuh"
 #include "sm100_util.cuh"
+#include "tmap.cuh"
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -872,22 +873,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- host side
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+using fer::host::EncodeTiledFn;
 
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
+EncodeTiledFn encode_fn() { return fer::host::encode_tiled_fn(); }
 
 // Tuning knobs read once per process: FERCUDA_GEMM_GROUP (256-row blocks
 // per raster group of the 2-CTA kernel) and FERCUDA_GEMM_L2_PROMOTION
