@@ -30,6 +30,7 @@
 // Every wait is bounded (about one second); on timeout the kernel records an
 // error bit, stops issuing work, releases tensor memory and returns.
 // No TMA multicast is used anywhere.
+#include "f32x2.cuh"
 #include "pdl.cuh"
 #include "sm100_util.cuh"
 #include "tmap.cuh"
@@ -156,31 +157,6 @@ __device__ __forceinline__ float gelu_erf(float x) {
     return __fmul_rn(__fmul_rn(0.5f, x), x < 0.0f ? s : __fsub_rn(2.0f, s));
 }
 
-// Two lanes of f32x2 (packed, one instruction per pair on sm_100).
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_splat(float v) { return f2_pack(v, v); }
 
 // gelu_erf of a pair, the same operations on packed f32x2 (bit-identical
 // to two scalar calls; about half the instructions in the epilogue).

@@ -26,6 +26,7 @@
 // misaligned base, cols > 16384) run a multi-pass kernel with the same
 // arithmetic.
 #include "elem.cuh"
+#include "f32x2.cuh"
 #include "sm100_util.cuh"
 
 #include <cuda_runtime.h>
@@ -195,17 +196,34 @@ __device__ __forceinline__ bool process_row_sb(float (&v)[VPT], const RowsArgs& 
         after_first_barrier();
         first = false;
         float s = 0.0f;
+        if constexpr (FULL && VPT % 2 == 0) {
+            // the subtractions and scalings in packed pairs (same bits)
 #pragma unroll
-        for (int j = 0; j < VPT; ++j)
-            if (FULL || t + kThreads * j < cols) {
-                v[j] = expf(v[j] - mx);
+            for (int j = 0; j < VPT; j += 2) {
+                f2_unpack(f2_sub(f2_pack(v[j], v[j + 1]), f2_splat(mx)), v[j], v[j + 1]);
+                v[j] = expf(v[j]);
                 s += v[j];
+                v[j + 1] = expf(v[j + 1]);
+                s += v[j + 1];
             }
+        } else {
+#pragma unroll
+            for (int j = 0; j < VPT; ++j)
+                if (FULL || t + kThreads * j < cols) {
+                    v[j] = expf(v[j] - mx);
+                    s += v[j];
+                }
+        }
         int dummy = 0;
         const float sum = tree ? sb_halving_sum(s, sl.ln_sum, 0, &dummy) : sb_softmax_sum(s, sl.warp_sum);
         const float inv = 1.0f / sum;
+        if constexpr (VPT % 2 == 0) {
 #pragma unroll
-        for (int j = 0; j < VPT; ++j) v[j] *= inv;
+            for (int j = 0; j < VPT; j += 2) f2_unpack(f2_mul(f2_pack(v[j], v[j + 1]), f2_splat(inv)), v[j], v[j + 1]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < VPT; ++j) v[j] *= inv;
+        }
     }
     if (a.flags & kLayerNorm) {
         const float n = static_cast<float>(cols);
@@ -222,17 +240,37 @@ __device__ __forceinline__ bool process_row_sb(float (&v)[VPT], const RowsArgs& 
             after_first_barrier();
         }
         float q = 0.0f;
+        if constexpr (FULL && VPT % 2 == 0) {
+            // v - mean and its square in packed pairs; the sum stays in
+            // element order (same bits); v keeps v - mean
 #pragma unroll
-        for (int j = 0; j < VPT; ++j)
-            if (FULL || t + kThreads * j < cols) {
-                const float d = v[j] - mean;
-                q += d * d;
+            for (int j = 0; j < VPT; j += 2) {
+                const uint64_t d = f2_sub(f2_pack(v[j], v[j + 1]), f2_splat(mean));
+                float d0, d1;
+                f2_unpack(f2_mul(d, d), d0, d1);
+                q += d0;
+                q += d1;
+                f2_unpack(d, v[j], v[j + 1]);
             }
+        } else {
+#pragma unroll
+            for (int j = 0; j < VPT; ++j)
+                if (FULL || t + kThreads * j < cols) {
+                    const float d = v[j] - mean;
+                    q += d * d;
+                }
+        }
         int dummy = 0;
         const float var = sb_halving_sum(q, (a.flags & kSoftmaxTree) ? sl.ln_sum : sl.ln_var, 0, &dummy) / n;
         const float inv_std = rsqrtf(var + a.eps);
+        if constexpr (FULL && VPT % 2 == 0) {
 #pragma unroll
-        for (int j = 0; j < VPT; ++j) v[j] = (v[j] - mean) * inv_std;
+            for (int j = 0; j < VPT; j += 2)
+                f2_unpack(f2_mul(f2_pack(v[j], v[j + 1]), f2_splat(inv_std)), v[j], v[j + 1]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < VPT; ++j) v[j] = (v[j] - mean) * inv_std;
+        }
         if (a.gamma || a.beta) {
 #pragma unroll
             for (int j = 0; j < VPT; ++j) {
