@@ -659,13 +659,18 @@ fer_status_t JitManager::internal_module(const std::string& source, std::shared_
 
 fer_status_t JitManager::chain_kernels(const fer_chain_op_t* ops, uint32_t n_ops, uint32_t n_inputs,
                                        const ChainKernels** out) {
+    // key: one byte per opcode (and the input index of a load), then the
+    // input count; short chains stay within std::string's inline buffer
     std::string sig;
     for (uint32_t i = 0; i < n_ops; ++i) {
-        sig += std::to_string(ops[i].opcode);
-        if (ops[i].opcode == FER_CHAIN_LOAD) sig += "." + std::to_string(ops[i].arg);
-        sig += ',';
+        if (ops[i].opcode > 126) return invalid("unknown chain opcode");
+        if (ops[i].opcode == FER_CHAIN_LOAD && ops[i].arg >= n_inputs)
+            return invalid("chain loads an input that was not bound");
+        sig += static_cast<char>(ops[i].opcode + 1);
+        if (ops[i].opcode == FER_CHAIN_LOAD) sig += static_cast<char>(ops[i].arg + 1);
     }
-    sig += "n" + std::to_string(n_inputs);
+    sig += static_cast<char>(0x7f);
+    sig += static_cast<char>(n_inputs);
     {
         std::lock_guard<std::mutex> lk(mu_);
         auto it = chains_.find(sig);

@@ -157,19 +157,53 @@ fer_status_t Session::add_buffer(const fer_buffer_desc_t& d, void* ptr, uint32_t
 // A caller that never polls its jobs would otherwise cost one
 // cudaEventCreate per submission: once 64 jobs are outstanding, the oldest
 // (by then normally complete) is finalized and its event reused.
+// Work on one stream completes in submission order, so once the event of a
+// pending job is complete, every older pending job recorded on the same
+// stream is complete too: one query retires up to kReclaimBatch jobs.
 void Session::reclaim_oldest() {
+    constexpr size_t kReclaimBatch = 32;
     while (!pending.empty()) {
         auto it = jobs.find(pending.front());
-        if (it == jobs.end() || it->second.finalized) {
-            pending.pop_front();
-            continue;
-        }
-        if (cudaEventQuery(it->second.ev) != cudaSuccess) return;
-        bool done = false;
-        finalize(it->first, &done);
+        if (it != jobs.end() && !it->second.finalized) break;
         pending.pop_front();
+    }
+    if (pending.empty()) return;
+    size_t k = (pending.size() < kReclaimBatch ? pending.size() : kReclaimBatch) - 1;
+    const Job* probe = nullptr;
+    for (;; --k) {
+        auto it = jobs.find(pending[k]);
+        if (it != jobs.end() && !it->second.finalized) {
+            probe = &it->second;
+            break;
+        }
+        if (k == 0) return;
+    }
+    const cudaStream_t st = probe->stream;
+    if (cudaEventQuery(probe->ev) != cudaSuccess) {
+        // the oldest alone may still be done
+        Job& j = jobs[pending.front()];
+        if (cudaEventQuery(j.ev) == cudaSuccess) {
+            finalize_done(j);
+            pending.pop_front();
+        }
         return;
     }
+    for (size_t i = 0; i <= k && !pending.empty(); ++i) {
+        auto it = jobs.find(pending.front());
+        if (it != jobs.end() && !it->second.finalized) {
+            if (it->second.stream != st) return;   // another stream: no ordering to rely on
+            finalize_done(it->second);
+        }
+        pending.pop_front();
+    }
+}
+
+void Session::finalize_done(Job& j) {
+    for (const Temp& t : j.temps) free_bytes(t.ptr, t.regime, t.tier, t.bytes);
+    j.temps.clear();
+    spare_events.push_back(j.ev);
+    j.ev = nullptr;
+    j.finalized = true;
 }
 
 fer_status_t Session::make_job(std::vector<Temp> temps, uint64_t* out_job) {
@@ -190,6 +224,7 @@ fer_status_t Session::make_job(std::vector<Temp> temps, uint64_t* out_job) {
     const uint64_t id = next_job++;
     Job& j = jobs[id];
     j.ev = ev;
+    j.stream = stream;
     j.temps = std::move(temps);
     pending.push_back(id);
     if (out_job) *out_job = id;
@@ -204,11 +239,7 @@ fer_status_t Session::finalize(uint64_t id, bool* done) {
     const cudaError_t q = cudaEventQuery(j.ev);
     if (q == cudaErrorNotReady) { *done = false; return ok(); }
     if (q != cudaSuccess) return internal("cudaEventQuery failed");
-    for (const Temp& t : j.temps) free_bytes(t.ptr, t.regime, t.tier, t.bytes);
-    j.temps.clear();
-    spare_events.push_back(j.ev);
-    j.ev = nullptr;
-    j.finalized = true;
+    finalize_done(j);
     *done = true;
     return ok();
 }

@@ -56,6 +56,7 @@ struct Temp {
 
 struct Job {
     cudaEvent_t ev = nullptr;   // null once finalized
+    cudaStream_t stream = nullptr;   // where ev was recorded
     std::vector<Temp> temps;
     bool finalized = false;
 };
@@ -108,8 +109,10 @@ struct Session {
     // Jobs: records completion of everything queued so far on the stream.
     fer_status_t make_job(std::vector<Temp> temps, uint64_t* out_job);
     fer_status_t finalize(uint64_t id, bool* done);
-    // Finalizes the oldest outstanding job if it has completed, returning its
-    // event to spare_events.
+    void finalize_done(Job& j);   // j's event has completed
+    // Finalizes completed outstanding jobs, oldest first (up to 32 per event
+    // query, relying on in-order completion on one stream), returning their
+    // events to spare_events.
     void reclaim_oldest();
 };
 
