@@ -206,7 +206,70 @@ void Session::finalize_done(Job& j) {
     j.finalized = true;
 }
 
+namespace {
+constexpr uint64_t kJobsPerEvent = 16;   // submissions that share one completion event at most
+}
+
+fer_status_t Session::close_open() {
+    if (!open_first) return ok();
+    cudaEvent_t ev = nullptr;
+    if (spare_events.empty() && pending.size() >= 64) reclaim_oldest();
+    if (!spare_events.empty()) {
+        ev = spare_events.back();
+        spare_events.pop_back();
+    } else if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+        return internal("cudaEventCreate failed");
+    }
+    if (cudaEventRecord(ev, open_stream) != cudaSuccess) {
+        spare_events.push_back(ev);
+        return internal("cudaEventRecord failed");
+    }
+    // the run is contiguous: every job since open_first was submitted on open_stream
+    const uint64_t last = next_job - 1;
+    Job& l = jobs[last];
+    l.ev = ev;
+    l.cover = last;
+    pending.push_back(last);
+    for (uint64_t id = open_first; id < last; ++id) {
+        auto it = jobs.find(id);
+        if (it != jobs.end()) it->second.cover = last;
+    }
+    open_first = 0;
+    return ok();
+}
+
+fer_status_t Session::cover_of(uint64_t id, uint64_t* out) {
+    auto it = jobs.find(id);
+    if (it == jobs.end()) return not_found("job id not found");
+    if (it->second.cover == 0) {
+        const fer_status_t st = close_open();
+        if (st.code != FER_STATUS_OK) return st;
+    }
+    *out = it->second.cover;
+    return ok();
+}
+
 fer_status_t Session::make_job(std::vector<Temp> temps, uint64_t* out_job) {
+    if (open_first && open_stream != stream) {
+        const fer_status_t st = close_open();
+        if (st.code != FER_STATUS_OK) {
+            for (const Temp& t : temps) free_bytes(t.ptr, t.regime, t.tier, t.bytes);
+            return st;
+        }
+    }
+    if (temps.empty()) {
+        const uint64_t id = next_job++;
+        Job& j = jobs[id];
+        j.stream = stream;
+        if (!open_first) {
+            open_first = id;
+            open_stream = stream;
+        }
+        if (out_job) *out_job = id;
+        // a failed record leaves the run open; a later query records it
+        if (id - open_first + 1 >= kJobsPerEvent) close_open();
+        return ok();
+    }
     cudaEvent_t ev = nullptr;
     if (spare_events.empty() && pending.size() >= 64) reclaim_oldest();
     if (!spare_events.empty()) {
@@ -225,8 +288,17 @@ fer_status_t Session::make_job(std::vector<Temp> temps, uint64_t* out_job) {
     Job& j = jobs[id];
     j.ev = ev;
     j.stream = stream;
+    j.cover = id;
     j.temps = std::move(temps);
     pending.push_back(id);
+    if (open_first) {
+        // an open run on this stream completes before this event
+        for (uint64_t k = open_first; k < id; ++k) {
+            auto it = jobs.find(k);
+            if (it != jobs.end()) it->second.cover = id;
+        }
+        open_first = 0;
+    }
     if (out_job) *out_job = id;
     return ok();
 }
@@ -236,6 +308,17 @@ fer_status_t Session::finalize(uint64_t id, bool* done) {
     if (it == jobs.end()) return not_found("job id not found");
     Job& j = it->second;
     if (j.finalized) { *done = true; return ok(); }
+    uint64_t c = 0;
+    fer_status_t st = cover_of(id, &c);
+    if (st.code != FER_STATUS_OK) return st;
+    if (c != id) {
+        bool cd = false;
+        st = finalize(c, &cd);
+        if (st.code != FER_STATUS_OK) return st;
+        if (cd) j.finalized = true;
+        *done = cd;
+        return ok();
+    }
     const cudaError_t q = cudaEventQuery(j.ev);
     if (q == cudaErrorNotReady) { *done = false; return ok(); }
     if (q != cudaSuccess) return internal("cudaEventQuery failed");
@@ -527,8 +610,13 @@ fer_status_t fer_job_wait(fer_session_t* session, uint64_t job_id) {
     FER_SESSION(session);
     auto it = S.jobs.find(job_id);
     if (it == S.jobs.end()) return not_found("job id not found");
-    if (!it->second.finalized && cudaEventSynchronize(it->second.ev) != cudaSuccess)
-        return internal("cudaEventSynchronize failed");
+    if (!it->second.finalized) {
+        uint64_t c = 0;
+        const fer_status_t st = S.cover_of(job_id, &c);
+        if (st.code != FER_STATUS_OK) return st;
+        const fer::capi::Job& cj = S.jobs[c];
+        if (!cj.finalized && cudaEventSynchronize(cj.ev) != cudaSuccess) return internal("cudaEventSynchronize failed");
+    }
     bool done = false;
     return S.finalize(job_id, &done);
 }

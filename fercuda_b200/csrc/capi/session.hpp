@@ -54,9 +54,14 @@ struct Temp {
     size_t bytes;
 };
 
+// A job without temporaries shares the completion event of a later job on
+// the same stream (`cover`, recorded at most 16 submissions later, or when
+// the job is queried, or when the stream changes); a job with temporaries,
+// and each covering job, records its own event (cover == its own id).
 struct Job {
-    cudaEvent_t ev = nullptr;   // null once finalized
-    cudaStream_t stream = nullptr;   // where ev was recorded
+    cudaEvent_t ev = nullptr;   // own event; null once finalized or when covered
+    cudaStream_t stream = nullptr;   // where the job was submitted
+    uint64_t cover = 0;         // job whose event covers this one; 0 while not yet recorded
     std::vector<Temp> temps;
     bool finalized = false;
 };
@@ -86,7 +91,9 @@ struct Session {
     std::unordered_map<uint64_t, Job> jobs;
     uint64_t next_job = 1;
     std::vector<cudaEvent_t> spare_events;
-    std::deque<uint64_t> pending;    // jobs not yet finalized, oldest first
+    std::deque<uint64_t> pending;    // jobs with an event, not yet finalized, oldest first
+    uint64_t open_first = 0;         // first job of the run still waiting for an event (0: none)
+    cudaStream_t open_stream = nullptr;
     size_t live_bytes[2] = {0, 0};   // CUDA_MALLOC / MANAGED budget per tier
     uint32_t* dev_err = nullptr;     // device error word (cudaMalloc'd)
     std::unique_ptr<JitManager> jit;
@@ -110,6 +117,10 @@ struct Session {
     fer_status_t make_job(std::vector<Temp> temps, uint64_t* out_job);
     fer_status_t finalize(uint64_t id, bool* done);
     void finalize_done(Job& j);   // j's event has completed
+    // Records one event for the open run of jobs without their own event.
+    fer_status_t close_open();
+    // Job id whose event covers `id` (recording it first if needed).
+    fer_status_t cover_of(uint64_t id, uint64_t* out);
     // Finalizes completed outstanding jobs, oldest first (up to 32 per event
     // query, relying on in-order completion on one stream), returning their
     // events to spare_events.

@@ -327,6 +327,49 @@ def test_stream_handoff_and_jobs(session):
     assert st.code == capi.FER_STATUS_NOT_FOUND
 
 
+def test_jobs_share_completion_events(session):
+    """Jobs without temporaries share one completion event per run of up to
+    16 submissions. Every job must still report done only after its own work:
+    a job is waited on in the middle of a run, queried before and after, and
+    the stream is switched while a run is open (the run is recorded on the
+    stream it was submitted on)."""
+    torch = pytest.importorskip("torch")
+    n = 1 << 20
+    bx, by = session.alloc(capi.FER_DTYPE_F32, [n]), session.alloc(capi.FER_DTYPE_F32, [n])
+    session.upload(bx, np.ones(n, np.float32))
+    done = C.c_uint8()
+
+    def status(job):
+        capi.check("status", session.call("fer_job_status", C.c_uint64(job), C.byref(done)))
+        return done.value
+
+    jobs = [session.affine(bx, by, n, 2.0, float(k), 0) for k in range(40)]
+    assert jobs == list(range(jobs[0], jobs[0] + 40))
+    session.wait(jobs[20])                                 # inside the third run
+    assert all(status(j) == 1 for j in jobs[:21])
+    session.wait(jobs[-1])                                 # the open run is recorded here
+    assert all(status(j) == 1 for j in jobs)
+    y = np.empty(n, np.float32)
+    session.download(by, y)
+    assert np.all(y == 2.0 + 39.0)
+    # a run left open on one stream, then the session moves to another
+    old = session.stream()
+    s2 = torch.cuda.Stream()
+    first = [session.affine(bx, by, n, 1.0, 5.0, 0) for _ in range(3)]
+    capi.check("attach", session.call("fer_stream_attach", C.c_uint64(s2.cuda_stream)))
+    s2.wait_stream(torch.cuda.ExternalStream(old))         # the caller orders the two streams
+    second = session.affine(by, bx, n, 1.0, 1.0, 0)        # reads what the first run wrote
+    session.wait(second)
+    for j in first:
+        session.wait(j)
+    assert all(status(j) == 1 for j in first + [second])
+    session.download(bx, y)
+    assert np.all(y == 7.0)
+    capi.check("attach", session.call("fer_stream_attach", C.c_uint64(old)))
+    session.free(bx)
+    session.free(by)
+
+
 def test_regimes_cuda_malloc_budget():
     """CUDA_MALLOC regime honours the per-tier byte budget of the pool config."""
     with capi.Session(0, pool_bytes=128 << 20, regime=capi.FER_MEMORY_CUDA_MALLOC) as s:
