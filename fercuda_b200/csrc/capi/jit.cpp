@@ -329,14 +329,50 @@ fer_status_t chain_source(const fer_chain_op_t* ops, uint32_t n, uint32_t n_inpu
            "                                                      const FerChainParams& p) {\n"
            "  (void)i0; (void)i1; (void)i2; (void)i3;\n"
         << body.str() << "  return s0;\n}\n"
-        << "extern \"C\" __global__ void __launch_bounds__(256) fer_chain_v4(\n"
+        << "static __device__ __forceinline__ float4 fer_chain_eval4(float4 x0, float4 x1, float4 x2, float4 x3,\n"
+           "                                                       const FerChainParams& p) {\n"
+           "  float4 r;\n"
+           "  r.x = fer_chain_eval(x0.x, x1.x, x2.x, x3.x, p);\n"
+           "  r.y = fer_chain_eval(x0.y, x1.y, x2.y, x3.y, p);\n"
+           "  r.z = fer_chain_eval(x0.z, x1.z, x2.z, x3.z, p);\n"
+           "  r.w = fer_chain_eval(x0.w, x1.w, x2.w, x3.w, p);\n"
+           "  return r;\n}\n"
+           "// early 1: the host found that the kernel just before this one on the\n"
+           "// stream writes none of the inputs, so each thread's first two groups are\n"
+           "// loaded and evaluated before the dependency wait; their stores wait.\n"
+           "// early 2: that kernel also neither reads nor writes the output, so the\n"
+           "// two groups are stored before the wait too. Every thread still waits\n"
+           "// before it exits, so this kernel completes after that one.\n"
+           "extern \"C\" __global__ void __launch_bounds__(256) fer_chain_v4(\n"
            "    const float4* __restrict__ a0, const float4* __restrict__ a1, const float4* __restrict__ a2,\n"
-           "    const float4* __restrict__ a3, float4* __restrict__ out, unsigned long long n4, FerChainParams p) {\n"
-           "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
-           "  asm volatile(\"griddepcontrol.launch_dependents;\");\n"
+           "    const float4* __restrict__ a3, float4* __restrict__ out, unsigned long long n4, FerChainParams p,\n"
+           "    unsigned early) {\n"
            "  const unsigned long long stride = (unsigned long long)gridDim.x * 256ull;\n"
            "  unsigned long long i = (unsigned long long)blockIdx.x * 256ull + threadIdx.x;\n"
            "  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);\n"
+           "  float4 r0 = z, r1 = z;\n"
+           "  if (early) {\n"
+           "    if (i < n4)\n"
+           "      r0 = fer_chain_eval4(a0 ? __ldcs(a0 + i) : z, a1 ? __ldcs(a1 + i) : z, a2 ? __ldcs(a2 + i) : z,\n"
+           "                           a3 ? __ldcs(a3 + i) : z, p);\n"
+           "    const unsigned long long k = i + stride;\n"
+           "    if (k < n4)\n"
+           "      r1 = fer_chain_eval4(a0 ? __ldcs(a0 + k) : z, a1 ? __ldcs(a1 + k) : z, a2 ? __ldcs(a2 + k) : z,\n"
+           "                           a3 ? __ldcs(a3 + k) : z, p);\n"
+           "  }\n"
+           "  if (early == 2u) {\n"
+           "    if (i < n4) __stcs(out + i, r0);\n"
+           "    if (i + stride < n4) __stcs(out + i + stride, r1);\n"
+           "  }\n"
+           "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
+           "  asm volatile(\"griddepcontrol.launch_dependents;\");\n"
+           "  if (early) {\n"
+           "    if (early == 1u) {\n"
+           "      if (i < n4) __stcs(out + i, r0);\n"
+           "      if (i + stride < n4) __stcs(out + i + stride, r1);\n"
+           "    }\n"
+           "    i += 2ull * stride;\n"
+           "  }\n"
            "  for (; i + 3ull * stride < n4; i += 4ull * stride) {\n"
            "    float4 x0[4], x1[4], x2[4], x3[4];\n"
            "#pragma unroll\n"
@@ -706,6 +742,10 @@ fer_status_t JitManager::chain_kernels(const fer_chain_op_t* ops, uint32_t n_ops
 
 // ============================================================ C entry points
 
+// Process-wide count of programmatic launches (libptx_kernels.so).
+extern "C" uint64_t fer_pdl_launch_count();
+extern "C" void fer_pdl_note_launch();
+
 namespace {
 
 int sm_count() {
@@ -723,12 +763,26 @@ int sm_count() {
 // previous kernel on the stream drains; the chain kernels begin with
 // griddepcontrol.wait, which holds them until that kernel has completed and
 // its writes are visible, so only the launch latency overlaps.
-cudaError_t launch_pdl(const void* fn, unsigned grid, void** args, cudaStream_t stream) {
+bool chain_pdl_enabled() {
     static const bool pdl = [] {
         const char* e = std::getenv("FERCUDA_CHAIN_PDL");   // 0: plain launches
         return !(e && e[0] == '0');
     }();
-    if (!pdl) return cudaLaunchKernel(fn, dim3(grid), dim3(256), args, 0, stream);
+    return pdl;
+}
+
+// FERCUDA_CHAIN_EARLY=0: the chain kernel never reads before its wait.
+bool chain_early_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("FERCUDA_CHAIN_EARLY");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+cudaError_t launch_pdl(const void* fn, unsigned grid, void** args, cudaStream_t stream) {
+    if (!chain_pdl_enabled()) return cudaLaunchKernel(fn, dim3(grid), dim3(256), args, 0, stream);
+    fer_pdl_note_launch();
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(256);
@@ -757,12 +811,37 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
         if (reinterpret_cast<uintptr_t>(in[i]) & 15u) aligned = false;
     }
     const uint64_t cap = static_cast<uint64_t>(sm_count()) * 8;
+    // Work before the dependency wait is safe when the kernel just before this
+    // one on the stream is the previous chain launch of this session (no
+    // other programmatic launch anywhere in the process since): reads when it
+    // wrote none of the inputs (early 1), stores too when it also neither
+    // read nor wrote the output (early 2). Any other predecessor either is
+    // not programmatic (this kernel starts only after it completes) or shows
+    // up in the launch count.
+    unsigned early = 0;
+    const uintptr_t out_lo = reinterpret_cast<uintptr_t>(out), out_hi = out_lo + n * sizeof(float);
+    auto overlaps = [](uintptr_t a0, uintptr_t a1, uintptr_t b0, uintptr_t b1) { return a0 < b1 && b0 < a1; };
+    if (chain_pdl_enabled() && chain_early_enabled() && S.chain_valid && S.chain_stream == S.stream &&
+        S.chain_mark == fer_pdl_launch_count()) {
+        early = 2;
+        for (uint32_t i = 0; i < n_inputs; ++i) {
+            const uintptr_t lo = reinterpret_cast<uintptr_t>(in[i]), hi = lo + n * sizeof(float);
+            if (overlaps(lo, hi, S.chain_out_lo, S.chain_out_hi)) early = 0;
+        }
+        if (early == 2) {
+            bool clash = overlaps(out_lo, out_hi, S.chain_out_lo, S.chain_out_hi);
+            for (uint32_t i = 0; i < S.chain_n_in; ++i)
+                clash = clash || overlaps(out_lo, out_hi, S.chain_in_lo[i], S.chain_in_hi[i]);
+            if (clash) early = 1;
+        }
+    }
+    S.chain_valid = false;
     uint64_t done = 0;
     if (aligned && n >= 4) {
         unsigned long long n4 = n / 4;
-        uint64_t g = (n4 + 255) / 256;
+        uint64_t g = (n4 + 511) / 512;   // two groups per thread before the wait
         if (g > cap) g = cap;
-        void* args[] = {&a[0], &a[1], &a[2], &a[3], &out, &n4, &p};
+        void* args[] = {&a[0], &a[1], &a[2], &a[3], &out, &n4, &p, &early};
         if (launch_pdl(reinterpret_cast<const void*>(ck.v4), static_cast<unsigned>(g), args, S.stream) !=
             cudaSuccess) {
             cudaGetLastError();
@@ -780,6 +859,16 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
             cudaGetLastError();
             return internal("kernel launch failed");
         }
+    }
+    S.chain_valid = true;
+    S.chain_stream = S.stream;
+    S.chain_mark = fer_pdl_launch_count();
+    S.chain_out_lo = out_lo;
+    S.chain_out_hi = out_hi;
+    S.chain_n_in = n_inputs;
+    for (uint32_t i = 0; i < n_inputs; ++i) {
+        S.chain_in_lo[i] = reinterpret_cast<uintptr_t>(in[i]);
+        S.chain_in_hi[i] = S.chain_in_lo[i] + n * sizeof(float);
     }
     return ok();
 }

@@ -94,6 +94,14 @@ struct Session {
     std::deque<uint64_t> pending;    // jobs with an event, not yet finalized, oldest first
     uint64_t open_first = 0;         // first job of the run still waiting for an event (0: none)
     cudaStream_t open_stream = nullptr;
+    // The last chain kernel launch: its stream, the bytes it read and wrote,
+    // and the process-wide programmatic launch count right after it.
+    bool chain_valid = false;
+    cudaStream_t chain_stream = nullptr;
+    uint64_t chain_mark = 0;
+    uintptr_t chain_out_lo = 0, chain_out_hi = 0;
+    uint32_t chain_n_in = 0;
+    uintptr_t chain_in_lo[4] = {0, 0, 0, 0}, chain_in_hi[4] = {0, 0, 0, 0};
     size_t live_bytes[2] = {0, 0};   // CUDA_MALLOC / MANAGED budget per tier
     uint32_t* dev_err = nullptr;     // device error word (cudaMalloc'd)
     std::unique_ptr<JitManager> jit;

@@ -18,6 +18,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <cstdlib>
 #include <utility>
 
@@ -32,6 +33,10 @@ __device__ __forceinline__ void pdl_begin() {
 }
 
 }  // namespace fer::dev
+
+// Process-wide count of programmatic launches (kernels/pdl.cu).
+extern "C" uint64_t fer_pdl_launch_count();
+extern "C" void fer_pdl_note_launch();
 
 namespace fer::host {
 
@@ -56,6 +61,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    if (cfg.numAttrs) fer_pdl_note_launch();
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
