@@ -760,9 +760,10 @@ int sm_count() {
 }
 
 // Programmatic dependent launch: the kernel may be scheduled while the
-// previous kernel on the stream drains; the chain kernels begin with
-// griddepcontrol.wait, which holds them until that kernel has completed and
-// its writes are visible, so only the launch latency overlaps.
+// previous kernel on the stream drains. The chain kernels wait
+// (griddepcontrol.wait) for that kernel to complete and its writes to be
+// visible before any memory access the host has not cleared (launch_chain's
+// `early`), and every thread waits before it exits.
 bool chain_pdl_enabled() {
     static const bool pdl = [] {
         const char* e = std::getenv("FERCUDA_CHAIN_PDL");   // 0: plain launches
