@@ -742,10 +742,6 @@ fer_status_t JitManager::chain_kernels(const fer_chain_op_t* ops, uint32_t n_ops
 
 // ============================================================ C entry points
 
-// Process-wide count of programmatic launches (libptx_kernels.so).
-extern "C" uint64_t fer_pdl_launch_count();
-extern "C" void fer_pdl_note_launch();
-
 namespace {
 
 int sm_count() {
@@ -782,8 +778,8 @@ bool chain_early_enabled() {
 }
 
 cudaError_t launch_pdl(const void* fn, unsigned grid, void** args, cudaStream_t stream) {
+    fer_pdl_note_launch();   // the chain kernels trigger their dependents however they are launched
     if (!chain_pdl_enabled()) return cudaLaunchKernel(fn, dim3(grid), dim3(256), args, 0, stream);
-    fer_pdl_note_launch();
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(256);
@@ -812,31 +808,17 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
         if (reinterpret_cast<uintptr_t>(in[i]) & 15u) aligned = false;
     }
     const uint64_t cap = static_cast<uint64_t>(sm_count()) * 8;
-    // Work before the dependency wait is safe when the kernel just before this
-    // one on the stream is the previous chain launch of this session (no
-    // other programmatic launch anywhere in the process since): reads when it
-    // wrote none of the inputs (early 1), stores too when it also neither
-    // read nor wrote the output (early 2). Any other predecessor either is
-    // not programmatic (this kernel starts only after it completes) or shows
-    // up in the launch count.
-    unsigned early = 0;
-    const uintptr_t out_lo = reinterpret_cast<uintptr_t>(out), out_hi = out_lo + n * sizeof(float);
-    auto overlaps = [](uintptr_t a0, uintptr_t a1, uintptr_t b0, uintptr_t b1) { return a0 < b1 && b0 < a1; };
-    if (chain_pdl_enabled() && chain_early_enabled() && S.chain_valid && S.chain_stream == S.stream &&
-        S.chain_mark == fer_pdl_launch_count()) {
-        early = 2;
-        for (uint32_t i = 0; i < n_inputs; ++i) {
-            const uintptr_t lo = reinterpret_cast<uintptr_t>(in[i]), hi = lo + n * sizeof(float);
-            if (overlaps(lo, hi, S.chain_out_lo, S.chain_out_hi)) early = 0;
-        }
-        if (early == 2) {
-            bool clash = overlaps(out_lo, out_hi, S.chain_out_lo, S.chain_out_hi);
-            for (uint32_t i = 0; i < S.chain_n_in; ++i)
-                clash = clash || overlaps(out_lo, out_hi, S.chain_in_lo[i], S.chain_in_hi[i]);
-            if (clash) early = 1;
-        }
+    // Work before the dependency wait: see Session::pdl_early.
+    uintptr_t in_lo[4] = {0, 0, 0, 0}, in_hi[4] = {0, 0, 0, 0};
+    for (uint32_t i = 0; i < n_inputs; ++i) {
+        in_lo[i] = reinterpret_cast<uintptr_t>(in[i]);
+        in_hi[i] = in_lo[i] + n * sizeof(float);
     }
-    S.chain_valid = false;
+    const uintptr_t out_lo = reinterpret_cast<uintptr_t>(out), out_hi = out_lo + n * sizeof(float);
+    unsigned early = (chain_pdl_enabled() && chain_early_enabled())
+                         ? S.pdl_early(in_lo, in_hi, n_inputs, out_lo, out_hi)
+                         : 0u;
+    S.last_pdl.valid = false;
     uint64_t done = 0;
     if (aligned && n >= 4) {
         unsigned long long n4 = n / 4;
@@ -861,16 +843,7 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
             return internal("kernel launch failed");
         }
     }
-    S.chain_valid = true;
-    S.chain_stream = S.stream;
-    S.chain_mark = fer_pdl_launch_count();
-    S.chain_out_lo = out_lo;
-    S.chain_out_hi = out_hi;
-    S.chain_n_in = n_inputs;
-    for (uint32_t i = 0; i < n_inputs; ++i) {
-        S.chain_in_lo[i] = reinterpret_cast<uintptr_t>(in[i]);
-        S.chain_in_hi[i] = S.chain_in_lo[i] + n * sizeof(float);
-    }
+    S.pdl_record(in_lo, in_hi, n_inputs, out_lo, out_hi);
     return ok();
 }
 

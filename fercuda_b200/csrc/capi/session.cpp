@@ -303,6 +303,34 @@ fer_status_t Session::make_job(std::vector<Temp> temps, uint64_t* out_job) {
     return ok();
 }
 
+unsigned Session::pdl_early(const uintptr_t* in_lo, const uintptr_t* in_hi, uint32_t n_in, uintptr_t out_lo,
+                            uintptr_t out_hi) const {
+    const PdlOp& p = last_pdl;
+    if (!p.valid || p.stream != stream || p.mark != fer_pdl_launch_count()) return 0;
+    auto overlaps = [](uintptr_t a0, uintptr_t a1, uintptr_t b0, uintptr_t b1) { return a0 < b1 && b0 < a1; };
+    for (uint32_t i = 0; i < n_in; ++i)
+        if (overlaps(in_lo[i], in_hi[i], p.out_lo, p.out_hi)) return 0;
+    if (overlaps(out_lo, out_hi, p.out_lo, p.out_hi)) return 1;
+    for (uint32_t i = 0; i < p.n_in; ++i)
+        if (overlaps(out_lo, out_hi, p.in_lo[i], p.in_hi[i])) return 1;
+    return 2;
+}
+
+void Session::pdl_record(const uintptr_t* in_lo, const uintptr_t* in_hi, uint32_t n_in, uintptr_t out_lo,
+                         uintptr_t out_hi) {
+    PdlOp& p = last_pdl;
+    p.valid = true;
+    p.stream = stream;
+    p.mark = fer_pdl_launch_count();
+    p.n_in = n_in > 4 ? 4 : n_in;
+    for (uint32_t i = 0; i < p.n_in; ++i) {
+        p.in_lo[i] = in_lo[i];
+        p.in_hi[i] = in_hi[i];
+    }
+    p.out_lo = out_lo;
+    p.out_hi = out_hi;
+}
+
 fer_status_t Session::finalize(uint64_t id, bool* done) {
     auto it = jobs.find(id);
     if (it == jobs.end()) return not_found("job id not found");

@@ -26,6 +26,11 @@
 #include <unordered_map>
 #include <vector>
 
+// Process-wide count of launches of kernels that trigger their dependents
+// (libptx_kernels.so, kernels/pdl.cu).
+extern "C" uint64_t fer_pdl_launch_count();
+extern "C" void fer_pdl_note_launch();
+
 namespace fer::capi {
 
 inline fer_status_t ok() { return fer_status_t{FER_STATUS_OK, "ok"}; }
@@ -94,14 +99,30 @@ struct Session {
     std::deque<uint64_t> pending;    // jobs with an event, not yet finalized, oldest first
     uint64_t open_first = 0;         // first job of the run still waiting for an event (0: none)
     cudaStream_t open_stream = nullptr;
-    // The last chain kernel launch: its stream, the bytes it read and wrote,
-    // and the process-wide programmatic launch count right after it.
-    bool chain_valid = false;
-    cudaStream_t chain_stream = nullptr;
-    uint64_t chain_mark = 0;
-    uintptr_t chain_out_lo = 0, chain_out_hi = 0;
-    uint32_t chain_n_in = 0;
-    uintptr_t chain_in_lo[4] = {0, 0, 0, 0}, chain_in_hi[4] = {0, 0, 0, 0};
+    // The last kernel with a known footprint (chain and fast row kernels)
+    // this session launched: its stream, the bytes it read and wrote, and the
+    // process-wide count of dependent-triggering launches right after it.
+    struct PdlOp {
+        bool valid = false;
+        cudaStream_t stream = nullptr;
+        uint64_t mark = 0;
+        uint32_t n_in = 0;
+        uintptr_t in_lo[4] = {0, 0, 0, 0}, in_hi[4] = {0, 0, 0, 0};
+        uintptr_t out_lo = 0, out_hi = 0;
+    } last_pdl;
+    // How much of a kernel reading [in_lo[i], in_hi[i]) and writing
+    // [out_lo, out_hi) may run before its programmatic launch wait, if it is
+    // launched next on the session stream: 0 nothing, 1 its reads (the
+    // kernel before writes none of the inputs), 2 everything (that kernel
+    // also neither reads nor writes the output). Nonzero only when the
+    // kernel before is last_pdl: no launch of another kernel that triggers
+    // its dependents anywhere in the process since. A kernel that never
+    // triggers its dependents cannot be overlapped by the next one, so it
+    // needs no record.
+    unsigned pdl_early(const uintptr_t* in_lo, const uintptr_t* in_hi, uint32_t n_in, uintptr_t out_lo,
+                       uintptr_t out_hi) const;
+    void pdl_record(const uintptr_t* in_lo, const uintptr_t* in_hi, uint32_t n_in, uintptr_t out_lo,
+                    uintptr_t out_hi);
     size_t live_bytes[2] = {0, 0};   // CUDA_MALLOC / MANAGED budget per tier
     uint32_t* dev_err = nullptr;     // device error word (cudaMalloc'd)
     std::unique_ptr<JitManager> jit;
@@ -168,6 +189,8 @@ cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* ou
                         cudaStream_t s);
 cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
                               float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
+cudaError_t fer_rows_fast_f32_pdl(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
+                                  float eps, uint32_t flags, uint32_t early, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_attn_causal(const void* qkv, void* out, int B, int S, int d, int heads, cudaStream_t s);
 size_t fer_gemm_splitk_workspace_bytes(int M, int N, int K);
 cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, void* c, int M, int N, int K, int epi, int splits,

@@ -1184,7 +1184,7 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
             at[1].val.programmaticStreamSerializationAllowed = 1;
             cfg.attrs = at;
             cfg.numAttrs = fer::host::pdl_enabled() ? 2 : 1;
-            if (cfg.numAttrs == 2) fer_pdl_note_launch();
+            fer_pdl_note_launch();   // the kernel triggers its dependents either way
             // the C map is not used by the cluster form
             const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<true>, ma, mb, ma, M, N, K, epi, cs,
                                                      kps, c, b_static, err);

@@ -1,8 +1,11 @@
-// Process-wide count of kernels launched with programmatic dependent launch
-// by this library and libfercuda_capi.so. A caller that wants to read
-// memory before its own kernel's griddepcontrol.wait needs to know that the
-// kernel just before it on the stream is one whose writes it can account
-// for; any programmatic launch it did not see in between shows up here.
+// Process-wide count of launches, by this library and libfercuda_capi.so, of
+// kernels that trigger their dependents (griddepcontrol.launch_dependents),
+// with or without the programmatic launch attribute: a kernel launched with
+// the attribute after one of them may start before it completes. A caller
+// that wants to touch memory before its own kernel's griddepcontrol.wait
+// needs to know that the kernel just before it on the stream is one whose
+// footprint it can account for; any such launch it did not see in between
+// shows up here.
 #include <atomic>
 #include <cstdint>
 

@@ -61,7 +61,9 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    if (cfg.numAttrs) fer_pdl_note_launch();
+    // counted even without the attribute: the kernel still triggers its
+    // dependents, so a programmatic launch after it may start early
+    fer_pdl_note_launch();
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 

@@ -21,6 +21,7 @@
 // The order of additions is fixed by the shape alone, so outputs are
 // bit-identical run to run; against the reference order they differ by
 // rounding only (max relative error well under 1e-5 of the largest output).
+#include "pdl.cuh"
 #include "sm100_util.cuh"
 
 #include <cuda_runtime.h>
@@ -45,6 +46,10 @@ struct FastArgs {
     int cols;
     float eps;
     uint32_t flags;
+    // Work before the programmatic launch wait (the host cleared it against
+    // the kernel just before on the stream): 0 none, 1 the first row's
+    // loads, 2 everything (the wait then only orders completion).
+    uint32_t early;
 };
 
 __device__ __forceinline__ float ex2(float v) {
@@ -175,8 +180,10 @@ __global__ void __launch_bounds__(kT) rows_fast_kernel(FastArgs a) {
             if (FULL || c < a.n4) dst[k] = __ldcs(src + c);
         }
     };
+    if (a.early == 0) fer::dev::pdl_begin();
     int r = blockIdx.x;
     if (r < a.rows) load(r, nv);
+    if (a.early == 1) fer::dev::pdl_begin();
     for (int it = 0; r < a.rows; r += gridDim.x, ++it) {
         float4 v[V4];
 #pragma unroll
@@ -188,6 +195,7 @@ __global__ void __launch_bounds__(kT) rows_fast_kernel(FastArgs a) {
         for (int k = 0; k < V4; ++k)
             if (FULL || t + kT * k < a.n4) __stcs(dst + t + kT * k, v[k]);
     }
+    if (a.early == 2) fer::dev::pdl_begin();   // every thread waits before it exits
 }
 
 int sm_count() {
@@ -202,7 +210,7 @@ int sm_count() {
 }
 
 template <int V4, bool FULL>
-cudaError_t launch_fast(const FastArgs& a, uint32_t* err, cudaStream_t s) {
+cudaError_t launch_fast(const FastArgs& a, bool pdl, uint32_t* err, cudaStream_t s) {
     (void)err;
     static int per_sm = 0;
     if (!per_sm) {
@@ -212,8 +220,42 @@ cudaError_t launch_fast(const FastArgs& a, uint32_t* err, cudaStream_t s) {
     }
     int grid = sm_count() * per_sm;
     if (grid > a.rows) grid = a.rows;
+    if (pdl) {
+        const cudaError_t e = fer::host::launch_pdl(rows_fast_kernel<V4, FULL>, dim3(grid), dim3(kT), 0, s, a);
+        return e != cudaSuccess ? e : cudaGetLastError();
+    }
+    // a plain launch still triggers dependents (the kernel executes the
+    // trigger), so it counts as such a launch
+    fer_pdl_note_launch();
     rows_fast_kernel<V4, FULL><<<grid, kT, 0, s>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t rows_fast(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols, float eps,
+                      uint32_t flags, uint32_t early, bool pdl, uint32_t* err, cudaStream_t stream) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
+    if ((cols % 4) || cols > 8192 || x == y || mis(x) || mis(y) || (gamma && mis(gamma)) || (beta && mis(beta)))
+        return cudaErrorNotSupported;
+    if (!(flags & (kSoftmax | kLayerNorm)) || early > 2) return cudaErrorInvalidValue;
+    if (!pdl) early = 0;
+    FastArgs a{reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), gamma, beta, rows, cols / 4, cols,
+               eps, flags, early};
+    const int v4 = (cols / 4 + kT - 1) / kT;
+    const bool full = (cols / 4) % kT == 0;
+    if (full) {
+        switch (v4) {
+            case 1: return launch_fast<1, true>(a, pdl, err, stream);
+            case 2: return launch_fast<2, true>(a, pdl, err, stream);
+            case 4: return launch_fast<4, true>(a, pdl, err, stream);
+            case 8: return launch_fast<8, true>(a, pdl, err, stream);
+            default: break;
+        }
+    }
+    if (v4 <= 1) return launch_fast<1, false>(a, pdl, err, stream);
+    if (v4 <= 2) return launch_fast<2, false>(a, pdl, err, stream);
+    if (v4 <= 4) return launch_fast<4, false>(a, pdl, err, stream);
+    return launch_fast<8, false>(a, pdl, err, stream);
 }
 
 }  // namespace
@@ -223,26 +265,16 @@ cudaError_t launch_fast(const FastArgs& a, uint32_t* err, cudaStream_t s) {
 // 16-byte aligned. flags: 1 softmax, 2 layer norm, 3 both.
 extern "C" cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, const float* beta, int rows,
                                          int cols, float eps, uint32_t flags, uint32_t* err, cudaStream_t stream) {
-    if (rows <= 0 || cols <= 0) return cudaSuccess;
-    auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
-    if ((cols % 4) || cols > 8192 || x == y || mis(x) || mis(y) || (gamma && mis(gamma)) || (beta && mis(beta)))
-        return cudaErrorNotSupported;
-    if (!(flags & (kSoftmax | kLayerNorm))) return cudaErrorInvalidValue;
-    FastArgs a{reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), gamma, beta, rows, cols / 4, cols,
-               eps, flags};
-    const int v4 = (cols / 4 + kT - 1) / kT;
-    const bool full = (cols / 4) % kT == 0;
-    if (full) {
-        switch (v4) {
-            case 1: return launch_fast<1, true>(a, err, stream);
-            case 2: return launch_fast<2, true>(a, err, stream);
-            case 4: return launch_fast<4, true>(a, err, stream);
-            case 8: return launch_fast<8, true>(a, err, stream);
-            default: break;
-        }
-    }
-    if (v4 <= 1) return launch_fast<1, false>(a, err, stream);
-    if (v4 <= 2) return launch_fast<2, false>(a, err, stream);
-    if (v4 <= 4) return launch_fast<4, false>(a, err, stream);
-    return launch_fast<8, false>(a, err, stream);
+    return rows_fast(x, y, gamma, beta, rows, cols, eps, flags, 0, false, err, stream);
+}
+
+// The same with programmatic dependent launch: `early` (0, 1, 2) says how
+// much of the kernel may run before it waits for the kernel just before it on
+// the stream (1: the first row's loads; 2: everything) and is the caller's
+// promise: 1 needs that kernel to write none of x / gamma / beta, 2 also that
+// it neither reads nor writes y.
+extern "C" cudaError_t fer_rows_fast_f32_pdl(const float* x, float* y, const float* gamma, const float* beta, int rows,
+                                             int cols, float eps, uint32_t flags, uint32_t early, uint32_t* err,
+                                             cudaStream_t stream) {
+    return rows_fast(x, y, gamma, beta, rows, cols, eps, flags, early, true, err, stream);
 }

@@ -389,7 +389,7 @@ cudaError_t launch_decode_attn(const void* qkv_dec, void* k_cache, void* v_cache
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl && fer::host::pdl_enabled() ? 1 : 0;
-    if (cfg.numAttrs) fer_pdl_note_launch();
+    fer_pdl_note_launch();   // the kernel triggers its dependents either way
     const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attn, mk, mv, static_cast<const bf16*>(qkv_dec),
                                              static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache),
                                              static_cast<bf16*>(out), scratch, counters, d, heads, max_seq, n_keys,

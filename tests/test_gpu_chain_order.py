@@ -117,3 +117,54 @@ def test_fixed_hazard_patterns(session):
         assert np.array_equal(got, w.astype(np.float32))
     for buf in (A, B, C, D, E):
         session.free(buf)
+
+
+def replay(session, init, plan, sync_each):
+    """Runs `plan` (a list of ("rows", ops, src, dst) / ("chain", alpha,
+    beta, src, dst)) on fresh buffers holding `init`; returns their bytes."""
+    ids = [session.alloc(capi.FER_DTYPE_F32, list(a.shape)) for a in init]
+    for b, a in zip(ids, init):
+        session.upload(b, a)
+    job = 0
+    for step in plan:
+        if step[0] == "rows":
+            _, ops, src, dst = step
+            job = session.rows(ids[src], ids[dst], ops)
+        else:
+            _, alpha, beta, src, dst = step
+            job = session.chain([(capi.FER_CHAIN_LOAD, 0, 0.0, 0.0), (capi.FER_CHAIN_AFFINE, 0, alpha, beta)],
+                                [ids[src]], ids[dst])
+        if sync_each:
+            session.wait(job)
+    session.wait(job)
+    out = []
+    for b, a in zip(ids, init):
+        got = np.empty_like(a)
+        session.download(b, got)
+        out.append(got)
+        session.free(b)
+    return out
+
+
+@pytest.mark.parametrize("seed", [21, 22])
+def test_rows_and_chains_back_to_back_equal_synchronous_replay(session, seed):
+    """Fast row kernels and chain kernels in a random order with random
+    buffer reuse give the same bits back to back as with a wait after every
+    call (both kernels are deterministic)."""
+    rng = np.random.default_rng(seed)
+    rows, cols = 512, 1024
+    init = [rng.standard_normal((rows, cols)).astype(np.float32) for _ in range(4)]
+    fast = capi.FER_ROWS_FAST
+    plan = []
+    for _ in range(120):
+        src, dst = (int(v) for v in rng.integers(0, 4, 2))
+        if rng.random() < 0.5:
+            ops = int(rng.choice([capi.FER_ROWS_SOFTMAX, capi.FER_ROWS_LAYER_NORM,
+                                  capi.FER_ROWS_SOFTMAX | capi.FER_ROWS_LAYER_NORM])) | fast
+            plan.append(("rows", ops, src, dst))
+        else:
+            plan.append(("chain", float(rng.choice([1.0, -1.0, 0.5])), float(rng.integers(-2, 3)), src, dst))
+    a = replay(session, init, plan, sync_each=False)
+    b = replay(session, init, plan, sync_each=True)
+    for x, y in zip(a, b):
+        assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
