@@ -118,28 +118,27 @@ fer_status_t fer_submit_rows(fer_session_t* session, const fer_rows_request_t* r
             return invalid("gamma/beta must be f32 with cols elements");
         (k == 0 ? gamma : beta) = static_cast<const float*>(g->ptr);
     }
+    // programmatic launch; how much may run before the kernel waits for the
+    // one before it follows from their footprints (Session::pdl_early)
+    const size_t row_bytes = static_cast<size_t>(cols) * sizeof(float);
+    uintptr_t in_lo[3] = {reinterpret_cast<uintptr_t>(x->ptr), 0, 0}, in_hi[3] = {in_lo[0] + x->bytes, 0, 0};
+    uint32_t n_in = 1;
+    for (const float* g : {gamma, beta})
+        if (g) {
+            in_lo[n_in] = reinterpret_cast<uintptr_t>(g);
+            in_hi[n_in] = in_lo[n_in] + row_bytes;
+            ++n_in;
+        }
+    const uintptr_t out_lo = reinterpret_cast<uintptr_t>(o->ptr), out_hi = out_lo + o->bytes;
+    const uint32_t early = S.pdl_early(in_lo, in_hi, n_in, out_lo, out_hi);
     cudaError_t e = cudaErrorNotSupported;
-    if (req->ops & FER_ROWS_FAST) {
-        // programmatic launch; how much may run before the kernel waits for
-        // the one before it follows from their footprints (Session::pdl_early)
-        const size_t row_bytes = static_cast<size_t>(cols) * sizeof(float);
-        uintptr_t in_lo[3] = {reinterpret_cast<uintptr_t>(x->ptr), 0, 0}, in_hi[3] = {in_lo[0] + x->bytes, 0, 0};
-        uint32_t n_in = 1;
-        for (const float* g : {gamma, beta})
-            if (g) {
-                in_lo[n_in] = reinterpret_cast<uintptr_t>(g);
-                in_hi[n_in] = in_lo[n_in] + row_bytes;
-                ++n_in;
-            }
-        const uintptr_t out_lo = reinterpret_cast<uintptr_t>(o->ptr), out_hi = out_lo + o->bytes;
-        const uint32_t early = S.pdl_early(in_lo, in_hi, n_in, out_lo, out_hi);
+    if (req->ops & FER_ROWS_FAST)
         e = fer_rows_fast_f32_pdl(static_cast<const float*>(x->ptr), static_cast<float*>(o->ptr), gamma, beta, rows,
                                   cols, req->eps, ops, early, S.dev_err, S.stream);
-        if (e == cudaSuccess) S.pdl_record(in_lo, in_hi, n_in, out_lo, out_hi);
-    }
     if (e == cudaErrorNotSupported)
-        e = fer_rows_f32(static_cast<const float*>(x->ptr), static_cast<float*>(o->ptr), gamma, beta, rows, cols,
-                         req->eps, ops, S.dev_err, S.stream);
+        e = fer_rows_f32_pdl(static_cast<const float*>(x->ptr), static_cast<float*>(o->ptr), gamma, beta, rows, cols,
+                             req->eps, ops, early, S.dev_err, S.stream);
+    if (e == cudaSuccess) S.pdl_record(in_lo, in_hi, n_in, out_lo, out_hi);
     fer_status_t st = launched(e);
     if (st.code != FER_STATUS_OK) return st;
     uint64_t job = 0;

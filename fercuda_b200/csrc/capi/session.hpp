@@ -169,6 +169,8 @@ struct fer_session {
 extern "C" {
 cudaError_t fer_rows_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
                          float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
+cudaError_t fer_rows_f32_pdl(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
+                             float eps, uint32_t flags, uint32_t early, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_layer_norm_typed(const void* x, void* y, int rows, int cols, float eps, uint32_t dtype,
                                  uint32_t* err, cudaStream_t stream);
 cudaError_t fer_matmul_ref_order(const void* a, const void* b, void* c, int M, int K, int N, uint32_t dtype,

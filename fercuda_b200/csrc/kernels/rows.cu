@@ -27,6 +27,7 @@
 // arithmetic.
 #include "elem.cuh"
 #include "f32x2.cuh"
+#include "pdl.cuh"
 #include "sm100_util.cuh"
 
 #include <cuda_runtime.h>
@@ -59,6 +60,10 @@ struct RowsArgs {
     uint32_t flags;
     int stages;
     uint32_t* err;
+    // Bulk kernel only: work before the programmatic launch wait (cleared by
+    // the host against the kernel just before on the stream): 0 none, 1 the
+    // first ring fill, 2 everything (the wait then only orders completion).
+    uint32_t early;
 };
 
 __device__ __forceinline__ float warp_down_max(float v) {
@@ -305,6 +310,7 @@ __global__ void __launch_bounds__(kThreads) rows_bulk_kernel(RowsArgs a) {
         fence_mbar_init();
     }
     __syncthreads();
+    if (a.early == 0) pdl_begin();
     if (t == 0) {
         const int pre = my_rows < stages ? my_rows : stages;
         for (int i = 0; i < pre; ++i) {
@@ -313,6 +319,7 @@ __global__ void __launch_bounds__(kThreads) rows_bulk_kernel(RowsArgs a) {
             bulk_g2s(ring + static_cast<size_t>(i) * cols, a.x + r * cols, row_bytes, &full[i]);
         }
     }
+    if (a.early == 1) pdl_begin();
     for (int i = 0; i < my_rows; ++i) {
         const int s = i % stages;
         const uint32_t parity = static_cast<uint32_t>(i / stages) & 1u;
@@ -346,6 +353,7 @@ __global__ void __launch_bounds__(kThreads) rows_bulk_kernel(RowsArgs a) {
             if (FULL || c < cols) st_global_cs(out + c, v[j]);
         }
     }
+    if (a.early == 2) pdl_begin();   // every thread waits before it exits
 }
 
 // Any shape: one CTA per row, values re-read from global memory per pass,
@@ -508,8 +516,21 @@ int num_sms() {
     return g_num_sms;
 }
 
+// The bulk kernel triggers its dependents, so every launch is counted; with
+// `pdl` it is launched with the programmatic-serialization attribute.
 template <int VPT, bool FULL>
-cudaError_t launch_bulk(RowsArgs a, cudaStream_t stream) {
+cudaError_t go_bulk(const RowsArgs& a, int grid, size_t smem, bool pdl, cudaStream_t stream) {
+    if (pdl) {
+        const cudaError_t e = fer::host::launch_pdl(rows_bulk_kernel<VPT, FULL>, dim3(grid), dim3(kThreads), smem, stream, a);
+        return e != cudaSuccess ? e : cudaGetLastError();
+    }
+    fer_pdl_note_launch();
+    rows_bulk_kernel<VPT, FULL><<<grid, kThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+template <int VPT, bool FULL>
+cudaError_t launch_bulk(RowsArgs a, bool pdl, cudaStream_t stream) {
     const size_t row_bytes = static_cast<size_t>(a.cols) * 4;
     // Ring depth: the deepest ring among those that keep the most CTAs
     // resident per SM (2..8 row buffers). FERCUDA_ROWS_STAGES overrides it.
@@ -529,8 +550,7 @@ cudaError_t launch_bulk(RowsArgs a, cudaStream_t stream) {
             a.stages = cache[k].stages;
             int grid = num_sms() * cache[k].per_sm;
             if (grid > a.rows) grid = a.rows;
-            rows_bulk_kernel<VPT, FULL><<<grid, kThreads, row_bytes * a.stages, stream>>>(a);
-            return cudaGetLastError();
+            return go_bulk<VPT, FULL>(a, grid, row_bytes * a.stages, pdl, stream);
         }
     // The attribute is only an upper bound; occupancy follows the smem each
     // launch passes, so it is set once to the largest ring used.
@@ -556,7 +576,41 @@ cudaError_t launch_bulk(RowsArgs a, cudaStream_t stream) {
     if (cache_n < 8) cache[cache_n++] = Choice{dev, a.cols, best_stages, best_per_sm};
     int grid = num_sms() * best_per_sm;
     if (grid > a.rows) grid = a.rows;
-    rows_bulk_kernel<VPT, FULL><<<grid, kThreads, smem, stream>>>(a);
+    return go_bulk<VPT, FULL>(a, grid, smem, pdl, stream);
+}
+
+cudaError_t rows_launch(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols, float eps,
+                        uint32_t flags, uint32_t early, bool pdl, uint32_t* err, cudaStream_t stream) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    if (early > 2) return cudaErrorInvalidValue;
+    RowsArgs a{x, y, gamma, beta, rows, cols, eps, flags, 2, err, pdl ? early : 0u};
+    const bool bulk_ok = cols >= kThreads && cols <= 64 * kThreads && (cols % 4) == 0 &&
+                         (reinterpret_cast<uintptr_t>(x) % 16) == 0 && x != y;
+    if (bulk_ok) {
+        const int vpt = (cols + kThreads - 1) / kThreads;
+        const bool full = cols % kThreads == 0;
+        if (full) {
+            switch (vpt) {
+                case 1: return launch_bulk<1, true>(a, pdl, stream);
+                case 2: return launch_bulk<2, true>(a, pdl, stream);
+                case 4: return launch_bulk<4, true>(a, pdl, stream);
+                case 8: return launch_bulk<8, true>(a, pdl, stream);
+                case 16: return launch_bulk<16, true>(a, pdl, stream);
+                case 32: return launch_bulk<32, true>(a, pdl, stream);
+                case 64: return launch_bulk<64, true>(a, pdl, stream);
+                default: break;
+            }
+        }
+        if (vpt <= 2) return launch_bulk<2, false>(a, pdl, stream);
+        if (vpt <= 4) return launch_bulk<4, false>(a, pdl, stream);
+        if (vpt <= 8) return launch_bulk<8, false>(a, pdl, stream);
+        if (vpt <= 16) return launch_bulk<16, false>(a, pdl, stream);
+        if (vpt <= 32) return launch_bulk<32, false>(a, pdl, stream);
+        return launch_bulk<64, false>(a, pdl, stream);
+    }
+    // any other shape: the multi-pass kernel, plain launch, never triggers
+    int grid = rows < num_sms() * 8 ? rows : num_sms() * 8;
+    rows_generic_kernel<<<grid, kThreads, 0, stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -566,35 +620,16 @@ cudaError_t launch_bulk(RowsArgs a, cudaStream_t stream) {
 // flags: 1 = softmax, 2 = layer norm, 3 = softmax then layer norm.
 extern "C" cudaError_t fer_rows_f32(const float* x, float* y, const float* gamma, const float* beta, int rows,
                                     int cols, float eps, uint32_t flags, uint32_t* err, cudaStream_t stream) {
-    if (rows <= 0 || cols <= 0) return cudaSuccess;
-    RowsArgs a{x, y, gamma, beta, rows, cols, eps, flags, 2, err};
-    const bool bulk_ok = cols >= kThreads && cols <= 64 * kThreads && (cols % 4) == 0 &&
-                         (reinterpret_cast<uintptr_t>(x) % 16) == 0 && x != y;
-    if (bulk_ok) {
-        const int vpt = (cols + kThreads - 1) / kThreads;
-        const bool full = cols % kThreads == 0;
-        if (full) {
-            switch (vpt) {
-                case 1: return launch_bulk<1, true>(a, stream);
-                case 2: return launch_bulk<2, true>(a, stream);
-                case 4: return launch_bulk<4, true>(a, stream);
-                case 8: return launch_bulk<8, true>(a, stream);
-                case 16: return launch_bulk<16, true>(a, stream);
-                case 32: return launch_bulk<32, true>(a, stream);
-                case 64: return launch_bulk<64, true>(a, stream);
-                default: break;
-            }
-        }
-        if (vpt <= 2) return launch_bulk<2, false>(a, stream);
-        if (vpt <= 4) return launch_bulk<4, false>(a, stream);
-        if (vpt <= 8) return launch_bulk<8, false>(a, stream);
-        if (vpt <= 16) return launch_bulk<16, false>(a, stream);
-        if (vpt <= 32) return launch_bulk<32, false>(a, stream);
-        return launch_bulk<64, false>(a, stream);
-    }
-    int grid = rows < num_sms() * 8 ? rows : num_sms() * 8;
-    rows_generic_kernel<<<grid, kThreads, 0, stream>>>(a);
-    return cudaGetLastError();
+    return rows_launch(x, y, gamma, beta, rows, cols, eps, flags, 0, false, err, stream);
+}
+
+// The same with programmatic dependent launch where the bulk kernel applies;
+// `early` as fer_rows_fast_f32_pdl (1: the first ring fill, 2: the whole
+// kernel before the wait; the caller's promise about the kernel before).
+extern "C" cudaError_t fer_rows_f32_pdl(const float* x, float* y, const float* gamma, const float* beta, int rows,
+                                        int cols, float eps, uint32_t flags, uint32_t early, uint32_t* err,
+                                        cudaStream_t stream) {
+    return rows_launch(x, y, gamma, beta, rows, cols, eps, flags, early, true, err, stream);
 }
 
 // Layer norm of each row of a [rows, cols] buffer of dtype `dtype`

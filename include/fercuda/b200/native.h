@@ -77,13 +77,16 @@ cudaError_t fer_cast_from_f32(const float* in, void* out, size_t n, uint32_t dty
  * optional [cols] f32. fer_rows_f32: bit-identical to the reference kernels.
  * fer_rows_fast_f32: deterministic, within 1e-5 of the largest output of the
  * reference order; cudaErrorNotSupported for cols % 4 != 0, cols > 8192,
- * in-place or unaligned buffers. fer_rows_fast_f32_pdl: the same launched
- * with programmatic dependent launch; early 1 lets the first row's loads,
+ * in-place or unaligned buffers. fer_rows_f32_pdl / fer_rows_fast_f32_pdl:
+ * the same launched
+ * with programmatic dependent launch; early 1 lets the first loads,
  * early 2 the whole kernel run before it waits for the kernel just before it
  * on the stream (the caller promises that kernel writes none of x / gamma /
  * beta, and for 2 that it neither reads nor writes y). */
 cudaError_t fer_rows_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
                          float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
+cudaError_t fer_rows_f32_pdl(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
+                             float eps, uint32_t flags, uint32_t early, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
                               float eps, uint32_t flags, uint32_t* err, cudaStream_t stream);
 cudaError_t fer_rows_fast_f32_pdl(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,
