@@ -16,6 +16,7 @@
 // one chunk the CTA writes the result itself. Which CTA combines does not
 // change the arithmetic, and every reduction order depends only on len, so
 // results are bit-identical run to run.
+#include "f32x2.cuh"
 #include "pdl.cuh"
 #include "sm100_util.cuh"
 #include "tmap.cuh"
@@ -91,6 +92,11 @@ __device__ __forceinline__ void tma_load_rows(void* dst, const CUtensorMap* map,
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// The two bf16 of a 32-bit word as a packed f32 pair (low element first).
+__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) {
+    return fer::dev::f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 // Address of 16-byte piece c of row r in a 128-byte-swizzled stage.
 __device__ __forceinline__ int swz(int r, int c) { return r * kRowBytes + ((c ^ (r & 7)) << 4); }
 
@@ -98,8 +104,9 @@ __device__ __forceinline__ int swz(int r, int c) { return r * kRowBytes + ((c ^ 
 // tmK / tmV are maps over the cache rows (box 64 x kSub, 128-byte swizzle),
 // so a stage of K and V is two TMA loads; kStages stages in flight.
 // Thread t = 4 * slot + qt owns key slot `slot` of every stage and dims
-// 16 qt .. 16 qt + 15: it adds its part of q.k (two 16-byte pieces, in dim
-// order), the four parts are added by a fixed butterfly (every lane of the
+// 16 qt .. 16 qt + 15: it adds its part of q.k (two 16-byte pieces; even and
+// odd dims in two packed f32x2 chains, in dim order, then added), the four
+// parts are added by a fixed butterfly (every lane of the
 // slot gets the same score), and the slot keeps its own running maximum m,
 // sum l and o[16 dims] (online softmax, rescaled when m grows). At the end
 // the 32 slots are combined in slot order.
@@ -180,9 +187,13 @@ __global__ void __launch_bounds__(kThreads) decode_attn(const __grid_constant__ 
         *reinterpret_cast<uint4*>((kv ? vc : kc) + (static_cast<size_t>(row0) + j_new) * HD + piece * 8) = new_piece;
     }
 
-    float m = -INFINITY, l = 0.0f, acc[16];
+    uint64_t q2[8];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+    for (int e = 0; e < 8; ++e) q2[e] = f2_pack(qr[2 * e], qr[2 * e + 1]);
+    float m = -INFINITY, l = 0.0f;
+    uint64_t acc2[8];   // o[16 dims] as packed pairs
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc2[e] = 0ull;
     for (int i = 0; i < nsub; ++i) {
         const int s_i = i % kStages;
         const bool ok = mbar_wait(&full[s_i], static_cast<uint32_t>(i / kStages) & 1u);
@@ -203,40 +214,37 @@ __global__ void __launch_bounds__(kThreads) decode_attn(const __grid_constant__ 
             __syncthreads();
         }
         const int j = i * kSub + slot;
-        float s = 0.0f;
+        uint64_t s2 = 0ull;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
             const uint4 u = lds128(sk + swz(slot, 2 * qt + cc));
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
-                s = fmaf(qr[8 * cc + 2 * e], f.x, s);
-                s = fmaf(qr[8 * cc + 2 * e + 1], f.y, s);
-            }
+            for (int e = 0; e < 4; ++e) s2 = f2_fma(q2[4 * cc + e], bf16x2_to_f2(w[e]), s2);
         }
+        float s_lo, s_hi;
+        f2_unpack(s2, s_lo, s_hi);
+        float s = s_lo + s_hi;
         s += __shfl_xor_sync(0xffffffffu, s, 1);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
         if (j < nk) {
             if (s > m) {
                 const float alpha = __expf(m - s);
                 l *= alpha;
+                const uint64_t a2 = f2_splat(alpha);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) acc[e] *= alpha;
+                for (int e = 0; e < 8; ++e) acc2[e] = f2_mul(acc2[e], a2);
                 m = s;
             }
             const float pj = __expf(s - m);
             l += pj;
+            const uint64_t p2 = f2_splat(pj);
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 const uint4 u = lds128(sv + swz(slot, 2 * qt + cc));
                 const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
-                    acc[8 * cc + 2 * e] = fmaf(pj, f.x, acc[8 * cc + 2 * e]);
-                    acc[8 * cc + 2 * e + 1] = fmaf(pj, f.y, acc[8 * cc + 2 * e + 1]);
-                }
+                for (int e = 0; e < 4; ++e) acc2[4 * cc + e] = f2_fma(p2, bf16x2_to_f2(w[e]), acc2[4 * cc + e]);
             }
         }
         if (has_new) fence_proxy_async_smem();            // a generic write may precede the stage's next load
@@ -248,6 +256,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn(const __grid_constant__ 
     float* so = reinterpret_cast<float*>(st);              // [32][64]
     float* sm = so + 32 * HD;                              // [32]
     float* sl = sm + 32;                                   // [32]
+    float acc[16];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f2_unpack(acc2[e], acc[2 * e], acc[2 * e + 1]);
 #pragma unroll
     for (int e = 0; e < 16; e += 4)
         *reinterpret_cast<float4*>(so + slot * HD + 16 * qt + e) = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
