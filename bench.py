@@ -632,7 +632,7 @@ def subresults(s, capi, synth, torch, stream):
     """Short measurements of the other workloads (one GPU)."""
     out = {}
     for name, cls, steps in (("softmax_layernorm", Rows, 50), ("softmax_layernorm_reference_order", Rows, 50),
-                             ("fused_elementwise", Chain, 200), ("gemm", Gemm, 10)):
+                             ("fused_elementwise", Chain, 2000), ("gemm", Gemm, 10)):
         wl = cls(s, capi, synth, exact=True) if name == "softmax_layernorm_reference_order" else cls(s, capi, synth)
         el = timed_steps(wl, torch, stream, steps, 5, None, 1)
         med = el / steps
