@@ -104,3 +104,39 @@ def test_conv2d_intent(session):
             ref[i, j] = np.einsum("hwc,fchw->f", patch, wi) + bvec
     ref = np.maximum(ref, 0.0)
     assert np.abs(y.reshape(oh, ow, F) - ref).max() < 1e-4
+
+
+def test_jobs_with_and_without_temporaries_interleaved(session):
+    """A reduce intent (a job with a temporary scratch buffer and its own
+    completion event) submitted inside a run of chain jobs (which share
+    events): every job reports done after a wait on it, the scratch is
+    released, and results follow stream order."""
+    n = 1 << 20
+    x = np.ones(n, np.float32)
+    bx, by, bo = (session.alloc(capi.FER_DTYPE_F32, [n]), session.alloc(capi.FER_DTYPE_F32, [n]),
+                  session.alloc(capi.FER_DTYPE_F32, [1]))
+    session.upload(bx, x)
+    session.upload(bo, np.zeros(1, np.float32))
+    jobs = [session.affine(bx, by, n, 1.0, float(k), 0) for k in range(5)]     # by = 1 + 4 at the end
+    b = capi.fer_jit_intent_bindings_t(by, bo, 0, 0)
+    red = C.c_uint64()
+    capi.check("intent", session.call("fer_jit_run_intent", C.byref(intent(capi.FER_JIT_INTENT_OP_REDUCE_SUM_F32, n)),
+                                      C.byref(b), C.byref(red)))
+    jobs += [session.affine(bx, bx, n, 2.0, 0.0, 0) for _ in range(3)]         # bx = 8 at the end
+    done = C.c_uint8()
+    session.wait(jobs[2])
+    for j in jobs[:5] + [red.value]:
+        capi.check("status", session.call("fer_job_status", C.c_uint64(j), C.byref(done)))
+    session.wait(red.value)
+    session.wait(jobs[-1])
+    for j in jobs + [red.value]:
+        capi.check("status", session.call("fer_job_status", C.c_uint64(j), C.byref(done)))
+        assert done.value == 1
+    o = np.empty(1, np.float32)
+    session.download(bo, o)
+    assert o[0] == np.float32(5.0 * n)
+    y = np.empty(n, np.float32)
+    session.download(bx, y)
+    assert np.all(y == 8.0)
+    for buf in (bx, by, bo):
+        session.free(buf)
