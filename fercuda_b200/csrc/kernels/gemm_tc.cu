@@ -570,17 +570,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col = nb * BN + c4 * 4;
             if (col >= N) continue;
             const uint32_t off = pbase + static_cast<uint32_t>((r * kPartStride + c4 * 4) * 4);
-            float4 acc = ld_cluster_f4(map_to_rank(off, 0));
-            int sp = 1;
-            // four splits' loads in flight, added in split order
-            for (; sp + 3 < splits; sp += 4) {
-                float4 v[4];
+            // every split's load in flight at once (splits <= 16), then the
+            // additions in split order
+            float4 v[16];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) v[u] = ld_cluster_f4(map_to_rank(off, static_cast<uint32_t>(sp + u)));
+            for (int u = 0; u < 16; ++u)
+                if (u < splits) v[u] = ld_cluster_f4(map_to_rank(off, static_cast<uint32_t>(u)));
+            float4 acc = v[0];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) add4(acc, v[u]);
-            }
-            for (; sp < splits; ++sp) add4(acc, ld_cluster_f4(map_to_rank(off, static_cast<uint32_t>(sp))));
+            for (int u = 1; u < 16; ++u)
+                if (u < splits) add4(acc, v[u]);
             splitk_store4(acc, out, (static_cast<size_t>(mb * BM + r) * N + col) / 4, epi);
         }
         cluster_sync_all();   // no CTA exits while its partial is still being read
