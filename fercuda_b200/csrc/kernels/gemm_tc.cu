@@ -855,14 +855,18 @@ EncodeTiledFn encode_fn() { return fer::host::encode_tiled_fn(); }
 // Tuning knobs read once per process: FERCUDA_GEMM_GROUP (256-row blocks
 // per raster group of the 2-CTA kernel) and FERCUDA_GEMM_L2_PROMOTION
 // (0 none, 1 64 B, 2 128 B, 3 256 B for the TMA loads).
-int gemm_group_m() {
-    static int g = 0;
-    if (!g) {
+// Default: GROUP_M2, or twice that for wide outputs (64 or more 256-column
+// tiles, e.g. an LM head), where a taller group re-reads the wide B operand
+// fewer times.
+int gemm_group_m(int num_n) {
+    static int g = -1;
+    if (g < 0) {
         const char* e = std::getenv("FERCUDA_GEMM_GROUP");
-        g = e ? std::atoi(e) : GROUP_M2;
-        if (g < 1) g = GROUP_M2;
+        g = e ? std::atoi(e) : 0;
+        if (g < 1) g = 0;
     }
-    return g;
+    if (g) return g;
+    return num_n >= 64 ? 2 * GROUP_M2 : GROUP_M2;
 }
 
 int l2_promotion() {
@@ -963,7 +967,7 @@ cudaError_t gemm_ex(const void* a, const void* b, void* c, const float* resid, i
             const int tiles2 = ((M + 255) / 256) * ((N + BN - 1) / BN);
             const int ncl = tiles2 < clusters ? tiles2 : clusters;
             gemm_bf16_tc2_kernel<<<2 * ncl, kThreads, SMEM2_BYTES, stream>>>(ma, mb, mc, M, N, K, epi,
-                                                                               gemm_group_m(), err);
+                                                                               gemm_group_m((N + BN - 1) / BN), err);
             return cudaGetLastError();
         }
     }
