@@ -53,7 +53,7 @@ def test_config2_full_size_vs_oracle_and_deterministic(session):
     oracle_lib.load().orc_softmax_layernorm_rows_f32(oracle_lib.ptr(x), oracle_lib.ptr(ref), rows, cols, EPS, 8)
     y1 = run(session, x, SM | LN | FAST)
     assert rel(y1, ref) <= TOL
-    for _ in range(2):
+    for _ in range(9):                      # ten runs in all, the same bits each time
         y2 = run(session, x, SM | LN | FAST)
         assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
 

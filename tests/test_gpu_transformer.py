@@ -160,3 +160,28 @@ def test_graph_replay_is_bit_identical_to_eager(session):
     session.free(bt)
     session.free(bl)
     m.close()
+
+
+def test_forward_bit_identical_over_ten_runs(session):
+    """Ten forwards of the same tokens (the first eager, the second captured,
+    the rest replayed, with 8-layer benchmark widths at a short sequence) give
+    the same logits bit for bit."""
+    L, d, h, F, V, B, S = 8, 1024, 16, 4096, 32000, 2, 128
+    m = capi.Transformer(session, L, d, h, F, V, B * S)
+    m.init_weights(4, 0.02)
+    bt = session.alloc(capi.FER_DTYPE_I32, [B, S])
+    bl = session.alloc(capi.FER_DTYPE_F32, [B, S, V])
+    session.upload(bt, tokens_for(B, S, V, 5))
+    first = None
+    for _ in range(10):
+        session.wait(m.forward(bt, bl))
+        y = np.empty((B, S, V), np.float32)
+        session.download(bl, y)
+        if first is None:
+            first = y
+        else:
+            assert np.array_equal(first.view(np.uint32), y.view(np.uint32))
+    assert session.device_errors() == 0
+    session.free(bt)
+    session.free(bl)
+    m.close()
