@@ -745,13 +745,12 @@ fer_status_t JitManager::chain_kernels(const fer_chain_op_t* ops, uint32_t n_ops
 namespace {
 
 int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
+    static const int n = [] {
+        int dev = 0, v = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
     return n;
 }
 

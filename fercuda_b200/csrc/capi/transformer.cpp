@@ -295,11 +295,10 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
         run(2, 0.0, [&] { return fer_ln_bf16(m->x, gf, bf, m->a, Ti, d, c.eps, st); });
         run(0, glm, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_lm, lb->ptr, nullptr, Ti, V, d, kEpiF32, err, st); });
     };
-    static int graphs_env = -1;
-    if (graphs_env < 0) {
+    static const int graphs_env = [] {
         const char* ev = std::getenv("FERCUDA_XFMR_GRAPH");
-        graphs_env = (ev && ev[0] == '0') ? 0 : 1;
-    }
+        return (ev && ev[0] == '0') ? 0 : 1;
+    }();
     Transformer::Graph* g = nullptr;
     if (!m->profiling && graphs_env && !m->graphs_off) {
         for (auto& x : m->graphs)
@@ -585,11 +584,10 @@ fer_status_t fer_transformer_decode(fer_session_t* session, uint64_t model, uint
         if (e == cudaSuccess) e = fer_device_int_add(kc.d_len, 1, st);
     };
     e = cudaMemcpyAsync(kc.tok_stage, tb->ptr, static_cast<size_t>(B) * sizeof(int), cudaMemcpyDeviceToDevice, st);
-    static int graphs_env = -1;
-    if (graphs_env < 0) {
+    static const int graphs_env = [] {
         const char* ev = std::getenv("FERCUDA_XFMR_GRAPH");
-        graphs_env = (ev && ev[0] == '0') ? 0 : 1;
-    }
+        return (ev && ev[0] == '0') ? 0 : 1;
+    }();
     const bool use_graph = graphs_env && !m->profiling && !m->graphs_off;
     if (e == cudaSuccess) {
         if (use_graph && kc.graph && kc.graph_batch == kc.batch) {

@@ -429,12 +429,9 @@ extern "C" cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorNotSupported;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(attn_causal_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static const cudaError_t attr_rc =
+        cudaFuncSetAttribute(attn_causal_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (attr_rc != cudaSuccess) return attr_rc;
     const float scale_log2 = 1.4426950408889634f / 8.0f;   // log2(e) / sqrt(64)
     const dim3 grid(S / TQ, heads, B);
     attn_causal_tc<<<grid, kThreads, SMEM_BYTES, stream>>>(tmq, tmkv, static_cast<__nv_bfloat16*>(out), S, d,

@@ -39,6 +39,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -859,23 +860,21 @@ EncodeTiledFn encode_fn() { return fer::host::encode_tiled_fn(); }
 // tiles, e.g. an LM head), where a taller group re-reads the wide B operand
 // fewer times.
 int gemm_group_m(int num_n) {
-    static int g = -1;
-    if (g < 0) {
+    static const int g = [] {
         const char* e = std::getenv("FERCUDA_GEMM_GROUP");
-        g = e ? std::atoi(e) : 0;
-        if (g < 1) g = 0;
-    }
+        const int v = e ? std::atoi(e) : 0;
+        return v < 1 ? 0 : v;
+    }();
     if (g) return g;
     return num_n >= 64 ? 2 * GROUP_M2 : GROUP_M2;
 }
 
 int l2_promotion() {
-    static int p = -1;
-    if (p < 0) {
+    static const int p = [] {
         const char* e = std::getenv("FERCUDA_GEMM_L2_PROMOTION");
-        p = e ? std::atoi(e) : static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
-        if (p < 0 || p > 3) p = static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
-    }
+        const int v = e ? std::atoi(e) : static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+        return (v < 0 || v > 3) ? static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B) : v;
+    }();
     return p;
 }
 
@@ -896,18 +895,17 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
 }
 
 int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
+    static const int n = [] {
+        int dev = 0, v = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
     return n;
 }
 
 int g_gemm_mode = 0;        // 0: 2-CTA kernel where it applies, 1: always the 1-CTA kernel
-int g_gemm_clusters = -1;   // co-resident 2-CTA clusters (queried once)
+std::atomic<int> g_gemm_clusters{-1};   // co-resident 2-CTA clusters (queried once; same value from any thread)
 
 }  // namespace
 
@@ -917,7 +915,7 @@ extern "C" void fer_gemm_tc_set_mode(int mode) { g_gemm_mode = mode; }
 
 // Number of 2-CTA clusters the persistent kernel launches at most (-1 before
 // the first 2-CTA GEMM on this device).
-extern "C" int fer_gemm_tc_clusters() { return g_gemm_clusters; }
+extern "C" int fer_gemm_tc_clusters() { return g_gemm_clusters.load(std::memory_order_relaxed); }
 
 // epi: 0 f32 out, 1 bf16 out, 2 bf16(gelu(acc)), 3 f32 out = resid + acc.
 // With resid == c the residual add happens in place (TMA reduce-add); any
@@ -949,7 +947,7 @@ cudaError_t gemm_ex(const void* a, const void* b, void* c, const float* resid, i
     }
     if (g_gemm_mode != 1 && M > BM) {
         // 2-CTA kernel: A boxes of 128 rows per CTA, one 256-row tile per cluster
-        int& clusters = g_gemm_clusters;
+        int clusters = g_gemm_clusters.load(std::memory_order_relaxed);
         if (clusters < 0) {
             cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  SMEM2_BYTES);
@@ -962,6 +960,7 @@ cudaError_t gemm_ex(const void* a, const void* b, void* c, const float* resid, i
             e = cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tc2_kernel, &cfg);
             clusters = (e == cudaSuccess && n > 0) ? n : 0;
             if (e != cudaSuccess) cudaGetLastError();
+            g_gemm_clusters.store(clusters, std::memory_order_relaxed);
         }
         if (clusters > 0) {
             const int tiles2 = ((M + 255) / 256) * ((N + BN - 1) / BN);
@@ -971,13 +970,9 @@ cudaError_t gemm_ex(const void* a, const void* b, void* c, const float* resid, i
             return cudaGetLastError();
         }
     }
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static const cudaError_t attr_rc = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (attr_rc != cudaSuccess) return attr_rc;
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
     const cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES,
@@ -1074,8 +1069,8 @@ int csplit_cap() {
 // Clusters of `size` CTAs of the cluster split-K kernel that can be resident
 // at once (0: none), queried once per size.
 int csplit_max_clusters(int size) {
-    static int cache[17] = {};
-    if (cache[size] == 0) {
+    static std::atomic<int> cache[17] = {};
+    if (cache[size].load(std::memory_order_relaxed) == 0) {
         int n = 0;
         cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              SMEM_BYTES);
@@ -1099,9 +1094,10 @@ int csplit_max_clusters(int size) {
             cudaGetLastError();
             n = 0;
         }
-        cache[size] = n > 0 ? n : -1;
+        cache[size].store(n > 0 ? n : -1, std::memory_order_relaxed);
     }
-    return cache[size] > 0 ? cache[size] : 0;
+    const int v = cache[size].load(std::memory_order_relaxed);
+    return v > 0 ? v : 0;
 }
 
 // Cluster split-K plan: the largest split count S <= 16 (each split whole
@@ -1205,13 +1201,9 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
         !make_map(&mc, ws, static_cast<uint64_t>(splits) * mpad, static_cast<uint64_t>(N), 32,
                   CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
         return cudaErrorInvalidValue;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static const cudaError_t attr_rc = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (attr_rc != cudaSuccess) return attr_rc;
     const int jobs = tiles * splits;
     const int grid = jobs < sm_count() ? jobs : sm_count();
     cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES, stream,

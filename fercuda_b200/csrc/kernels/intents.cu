@@ -11,6 +11,7 @@
 //   conv2d      one output per thread, accumulation order c, kh, kw with one
 //               fused multiply-add per tap (what the reference's NVRTC build,
 //               which contracts `acc += iv * wv`, computes).
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -136,26 +137,70 @@ extern "C" cudaError_t fer_conv2d_f32(const float* input, const float* weights, 
 //   - a process that has reserved nearly all device memory for its pools at
 //     start-up may have nothing left for cudaMalloc to return.
 // ptx_tensor_reduce_f32_noalloc serves them: the per-CTA partials live in the
-// fixed device array below, which every GPU that loads this library holds
-// until the process exits, so the call itself allocates nothing.
+// fixed device array below instead of allocated scratch, so the call itself
+// allocates nothing.
 //   - At most kNoAllocMaxPartials partials, i.e. n <= 33,554,432 elements;
 //     larger n is rejected with cudaErrorInvalidValue before any launch.
 //   - All calls share the array. Each call overwrites every partial it reads
 //     before reading it, so nothing needs clearing between calls; calls that
 //     overlap on the GPU (different streams, or several host threads) race
 //     on the array and must be serialised by the caller.
-//   - The first call on a device looks the array's device address up with
-//     cudaGetSymbolAddress (this device current). Make that first call before
-//     any stream capture begins.
+//   - Set-up, once per device and context: the first call with a device's
+//     context current loads this file's module (the 256 KiB array and the two
+//     reduction kernels, which lazy module loading would otherwise load on
+//     first launch) and looks the array's device address up with
+//     cudaGetSymbolAddress. Loading the module takes device memory, so that
+//     first call (a warm-up call will do) belongs before the caller reserves
+//     its memory, and before any stream capture. From then on the device
+//     holds the array until its context is destroyed.
+//   - The address is remembered per device together with the context's
+//     unique id (cuCtxGetId). After cudaDeviceReset, or any other teardown
+//     and re-creation of the context, the id differs and the next call
+//     repeats the set-up; that call again loads the module.
 constexpr unsigned kNoAllocMaxPartials = 65536;   // 256 KiB of f32 partials
 static __device__ __align__(256) float g_noalloc_partials[kNoAllocMaxPartials];
 
 namespace {
 
-std::mutex g_noalloc_mu;
-float* g_noalloc_addr[64] = {};
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-// Device address of g_noalloc_partials for the current device. In host code
+struct NoAllocSlot {
+    unsigned long long ctx_id = 0;   // 0: not set up (context ids start at 1)
+    float* addr = nullptr;
+};
+
+std::mutex g_noalloc_mu;
+NoAllocSlot g_noalloc_slot[64];
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+// Unique id of the context current on this thread (making the device's
+// primary context current first if none is). Caller holds g_noalloc_mu.
+cudaError_t current_context_id(int dev, unsigned long long* id) {
+    if (!g_ctx_get_current || !g_ctx_get_id) {
+        void* f0 = nullptr;
+        void* f1 = nullptr;
+        cudaDriverEntryPointQueryResult q0, q1;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f0, 12000, cudaEnableDefault, &q0);
+        if (e == cudaSuccess) e = cudaGetDriverEntryPointByVersion("cuCtxGetId", &f1, 12000, cudaEnableDefault, &q1);
+        if (e != cudaSuccess) return e;
+        if (q0 != cudaDriverEntryPointSuccess || q1 != cudaDriverEntryPointSuccess || !f0 || !f1)
+            return cudaErrorNotSupported;
+        g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f0);
+        g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f1);
+    }
+    CUcontext ctx = nullptr;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) return cudaErrorUnknown;
+    if (!ctx) {
+        const cudaError_t e = cudaSetDevice(dev);   // initialises and binds the primary context
+        if (e != cudaSuccess) return e;
+        if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx) return cudaErrorDeviceUninitialized;
+    }
+    return g_ctx_get_id(ctx, id) == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
+}
+
+// Device address of g_noalloc_partials in the current context. In host code
 // the symbol itself is only a host-side stand-in, so kernels get this address.
 cudaError_t noalloc_partials(float** out) {
     int dev = 0;
@@ -163,13 +208,23 @@ cudaError_t noalloc_partials(float** out) {
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
+    unsigned long long id = 0;
+    e = current_context_id(dev, &id);
+    if (e != cudaSuccess) return e;
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    if (slot.ctx_id != id || !slot.addr) {
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, reduce_stage1<false>);
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, reduce_stage2<false>);
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, reduce_stage1<true>);
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, reduce_stage2<true>);
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&p, g_noalloc_partials);
         if (e != cudaSuccess) return e;
-        g_noalloc_addr[dev] = static_cast<float*>(p);
+        slot.addr = static_cast<float*>(p);
+        slot.ctx_id = id;
     }
-    *out = g_noalloc_addr[dev];
+    *out = slot.addr;
     return cudaSuccess;
 }
 

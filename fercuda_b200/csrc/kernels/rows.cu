@@ -35,6 +35,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
+#include <mutex>
 
 namespace {
 
@@ -504,16 +505,14 @@ __global__ void __launch_bounds__(kThreads) ln_typed_kernel(const typename Elem<
     }
 }
 
-int g_num_sms = 0;
-
 int num_sms() {
-    if (g_num_sms == 0) {
-        int dev = 0;
+    static const int n = [] {
+        int dev = 0, v = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
-    }
-    return g_num_sms;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
+    return n;
 }
 
 // The bulk kernel triggers its dependents, so every launch is counted; with
@@ -534,24 +533,27 @@ cudaError_t launch_bulk(RowsArgs a, bool pdl, cudaStream_t stream) {
     const size_t row_bytes = static_cast<size_t>(a.cols) * 4;
     // Ring depth: the deepest ring among those that keep the most CTAs
     // resident per SM (2..8 row buffers). FERCUDA_ROWS_STAGES overrides it.
-    static int override_stages = -1;
-    if (override_stages < 0) {
+    static const int override_stages = [] {
         const char* e = std::getenv("FERCUDA_ROWS_STAGES");
-        override_stages = e ? std::atoi(e) : 0;
-    }
+        return e ? std::atoi(e) : 0;
+    }();
     // Decision cache per (device, cols) for this instantiation.
     struct Choice { int dev, cols, stages, per_sm; };
     static Choice cache[8] = {};
     static int cache_n = 0;
+    static std::mutex cache_mu;
     int dev = 0;
     cudaGetDevice(&dev);
-    for (int k = 0; k < cache_n; ++k)
-        if (cache[k].dev == dev && cache[k].cols == a.cols) {
-            a.stages = cache[k].stages;
-            int grid = num_sms() * cache[k].per_sm;
-            if (grid > a.rows) grid = a.rows;
-            return go_bulk<VPT, FULL>(a, grid, row_bytes * a.stages, pdl, stream);
-        }
+    {
+        std::lock_guard<std::mutex> lk(cache_mu);
+        for (int k = 0; k < cache_n; ++k)
+            if (cache[k].dev == dev && cache[k].cols == a.cols) {
+                a.stages = cache[k].stages;
+                int grid = num_sms() * cache[k].per_sm;
+                if (grid > a.rows) grid = a.rows;
+                return go_bulk<VPT, FULL>(a, grid, row_bytes * a.stages, pdl, stream);
+            }
+    }
     // The attribute is only an upper bound; occupancy follows the smem each
     // launch passes, so it is set once to the largest ring used.
     cudaError_t e = cudaFuncSetAttribute(rows_bulk_kernel<VPT, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -573,7 +575,10 @@ cudaError_t launch_bulk(RowsArgs a, bool pdl, cudaStream_t stream) {
     if (best_per_sm < 1) best_per_sm = 1;
     a.stages = best_stages;
     const size_t smem = row_bytes * best_stages;
-    if (cache_n < 8) cache[cache_n++] = Choice{dev, a.cols, best_stages, best_per_sm};
+    {
+        std::lock_guard<std::mutex> lk(cache_mu);
+        if (cache_n < 8) cache[cache_n++] = Choice{dev, a.cols, best_stages, best_per_sm};
+    }
     int grid = num_sms() * best_per_sm;
     if (grid > a.rows) grid = a.rows;
     return go_bulk<VPT, FULL>(a, grid, smem, pdl, stream);

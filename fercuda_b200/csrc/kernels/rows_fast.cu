@@ -199,25 +199,25 @@ __global__ void __launch_bounds__(kT) rows_fast_kernel(FastArgs a) {
 }
 
 int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
+    static const int n = [] {
+        int dev = 0, v = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
     return n;
 }
 
 template <int V4, bool FULL>
 cudaError_t launch_fast(const FastArgs& a, bool pdl, uint32_t* err, cudaStream_t s) {
     (void)err;
-    static int per_sm = 0;
-    if (!per_sm) {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_fast_kernel<V4, FULL>, kT, 0) != cudaSuccess ||
-            per_sm < 1)
-            per_sm = 1;
-    }
+    static const int per_sm = [] {
+        int v = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rows_fast_kernel<V4, FULL>, kT, 0) != cudaSuccess ||
+            v < 1)
+            v = 1;
+        return v;
+    }();
     int grid = sm_count() * per_sm;
     if (grid > a.rows) grid = a.rows;
     if (pdl) {

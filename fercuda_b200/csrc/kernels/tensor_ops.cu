@@ -39,13 +39,12 @@ struct alignas(sizeof(T) * E) Pack {
 };
 
 int sm_count() {
-    static int n = 0;
-    if (n == 0) {
-        int dev = 0;
+    static const int n = [] {
+        int dev = 0, v = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
     return n;
 }
 

@@ -5,8 +5,9 @@
 // computed there by libtorch); the GEMMs run on gemm_tc.cu.
 //
 //   fill_normal_bf16   seeded weight init on the device (counter-based
-//                      splitmix64 + Box-Muller), so a 333 MB model is made in
-//                      milliseconds and only rank 0's copy is broadcast
+//                      splitmix64 + Box-Muller, bit-identical to the host
+//                      generator), so a 333 MB model is made in milliseconds
+//                      and only rank 0's copy is broadcast
 //   embed_f32          token rows of the bf16 embedding -> f32 residual stream
 //   ln_bf16            per-token layer norm, f32 in, bf16 out (GEMM operand)
 //   attn_causal        causal multi-head attention for head_dim 64 straight out
@@ -36,15 +37,72 @@ __device__ __forceinline__ uint64_t splitmix_draw(uint64_t seed, uint64_t k) {
     return z ^ (z >> 31);
 }
 
-// Element i uses draws 2i+1 and 2i+2 of the seed's stream.
+// Box-Muller on draws 2i+1 and 2i+2 of the seed's stream for element i, with
+// ln and cos as fixed series evaluated by IEEE double +, -, *, /, sqrt, each
+// an explicit round-to-nearest intrinsic (no contraction into FMA), so the
+// bits equal the host generator's (fercuda_b200/synth.py normal_bf16) on any
+// IEEE machine that takes the same steps.
+//   ln(k 2^-53), 1 <= k <= 2^53: k = f 2^b, f in [sqrt(1/2), sqrt(2));
+//     ln = (b - 53) ln2 + 2 s P(s^2), s = (f - 1) / (f + 1), P the atanh series
+//   cos(2 pi k 2^-53), 0 <= k < 2^53: octant q = k >> 50, offset r (exact),
+//     odd octants take 1/8 - r; x = 2 pi r in [0, pi/4]; sin or cos series
+__constant__ double kLnSeries[11] = {
+    0x1.0000000000000p+0, 0x1.5555555555555p-2, 0x1.999999999999ap-3, 0x1.2492492492492p-3,
+    0x1.c71c71c71c71cp-4, 0x1.745d1745d1746p-4, 0x1.3b13b13b13b14p-4, 0x1.1111111111111p-4,
+    0x1.e1e1e1e1e1e1ep-5, 0x1.af286bca1af28p-5, 0x1.8618618618618p-5};
+__constant__ double kSinSeries[9] = {
+    0x1.0000000000000p+0, -0x1.5555555555555p-3, 0x1.1111111111111p-7, -0x1.a01a01a01a01ap-13,
+    0x1.71de3a556c734p-19, -0x1.ae64567f544e4p-26, 0x1.6124613a86d09p-33, -0x1.ae7f3e733b81fp-41,
+    0x1.952c77030ad4ap-49};
+__constant__ double kCosSeries[10] = {
+    0x1.0000000000000p+0, -0x1.0000000000000p-1, 0x1.5555555555555p-5, -0x1.6c16c16c16c17p-10,
+    0x1.a01a01a01a01ap-16, -0x1.27e4fb7789f5cp-22, 0x1.1eed8eff8d898p-29, -0x1.93974a8c07c9dp-37,
+    0x1.ae7f3e733b81fp-45, -0x1.6827863b97d97p-53};
+constexpr double kLn2 = 0x1.62e42fefa39efp-1;
+constexpr double kTwoPi = 0x1.921fb54442d18p+2;
+constexpr double kSqrtHalf = 0x1.6a09e667f3bcdp-1;
+
+template <int N>
+__device__ __forceinline__ double horner(const double (&c)[N], double t) {
+    double p = c[N - 1];
+#pragma unroll
+    for (int k = N - 2; k >= 0; --k) p = __dadd_rn(__dmul_rn(p, t), c[k]);
+    return p;
+}
+
+__device__ __forceinline__ double portable_ln(uint64_t k) {
+    const long long bits = __double_as_longlong(__ull2double_rn(k));      // exact: k <= 2^53
+    double e = static_cast<double>(static_cast<int>((bits >> 52) & 0x7ff) - 1075);
+    double f = __longlong_as_double((bits & 0x000fffffffffffffll) | (1022ll << 52));   // [0.5, 1)
+    if (f < kSqrtHalf) {
+        f = __dmul_rn(f, 2.0);
+        e = __dadd_rn(e, -1.0);
+    }
+    const double s = __ddiv_rn(__dadd_rn(f, -1.0), __dadd_rn(f, 1.0));
+    const double p = horner(kLnSeries, __dmul_rn(s, s));
+    return __dadd_rn(__dmul_rn(e, kLn2), __dmul_rn(__dmul_rn(2.0, s), p));
+}
+
+__device__ __forceinline__ double portable_cos_turns(uint64_t k) {
+    const int q = static_cast<int>(k >> 50);
+    double r = __dmul_rn(__ull2double_rn(k & ((1ull << 50) - 1)), 0x1p-53);
+    if (q & 1) r = __dadd_rn(0.125, -r);
+    const double x = __dmul_rn(kTwoPi, r);
+    const double x2 = __dmul_rn(x, x);
+    const bool use_cos = q == 0 || q == 3 || q == 4 || q == 7;
+    const double v = use_cos ? horner(kCosSeries, x2) : __dmul_rn(x, horner(kSinSeries, x2));
+    return (q >= 2 && q <= 5) ? -v : v;
+}
+
 __global__ void fill_normal_bf16(bf16* out, size_t n, uint64_t seed, float stddev) {
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const double sd = static_cast<double>(stddev);
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         const uint64_t d0 = splitmix_draw(seed, 2 * i + 1), d1 = splitmix_draw(seed, 2 * i + 2);
-        const float u1 = (static_cast<float>(d0 >> 40) + 1.0f) * 5.9604644775390625e-08f;   // (0, 1]
-        const float u2 = static_cast<float>(d1 >> 40) * 5.9604644775390625e-08f;            // [0, 1)
-        const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
-        out[i] = __float2bfloat16_rn(stddev * z);
+        const double z = __dmul_rn(__dsqrt_rn(__dmul_rn(-2.0, portable_ln((d0 >> 11) + 1))),
+                                   portable_cos_turns(d1 >> 11));
+        // mean 0 added as the host does (turns a -0 product into +0)
+        out[i] = __float2bfloat16_rn(__double2float_rn(__dadd_rn(0.0, __dmul_rn(sd, z))));
     }
 }
 

@@ -5,14 +5,24 @@ Generator: splitmix64 with the workload's seed. The k-th draw (k = 1, 2, ...)
 is mix(seed + k * 0x9E3779B97F4A7C15), so streams are computed in bulk.
   uniform01  = (draw >> 40) * 2^-24                 (24-bit, in [0, 1))
   uniform    = lo + (hi - lo) * uniform01, in float64, rounded once to f32
-  normal     = Box-Muller in float64 on two draws per sample:
+  normal     = Box-Muller in float64 on draws 2i+1, 2i+2 for sample i:
                u1 = ((d0 >> 11) + 1) * 2^-53, u2 = (d1 >> 11) * 2^-53,
                z = sqrt(-2 ln u1) * cos(2 pi u2); mean + std * z rounded once
+               to f32 (mean and std are taken as f32 values)
   bf16       = round-to-nearest-even of that float32
+
+ln and cos are this module's own series (portable_ln, portable_cos_turns),
+evaluated with IEEE float64 +, -, *, / and sqrt only, each rounded to
+nearest, in a fixed order. Any IEEE machine that follows the same steps
+without contracting a multiply and an add therefore gets the same bits: the
+device fill of the transformer weights (kernels/xfmr_kernels.cu,
+fill_normal_bf16) reproduces normal_bf16 exactly, which is what lets a
+fixture computed on the host pin the device forward.
 """
 from __future__ import annotations
 
 import math
+import os
 
 import numpy as np
 
@@ -40,15 +50,99 @@ def uniform_f32(seed: int, n: int, lo: float, hi: float) -> np.ndarray:
     return (lo + (hi - lo) * uniform01(seed, n)).astype(np.float32)
 
 
-def normal_f32(seed: int, n: int, mean: float = 0.0, std: float = 1.0, chunk: int = 1 << 24) -> np.ndarray:
+# Series coefficients, correctly rounded: 1/(2k+1) for ln (atanh series),
+# (-1)^k/(2k+1)! for sin, (-1)^k/(2k)! for cos. The device kernel carries the
+# same values as hexadecimal literals.
+LN_SERIES = tuple(float.fromhex(h) for h in (
+    "0x1.0000000000000p+0", "0x1.5555555555555p-2", "0x1.999999999999ap-3", "0x1.2492492492492p-3",
+    "0x1.c71c71c71c71cp-4", "0x1.745d1745d1746p-4", "0x1.3b13b13b13b14p-4", "0x1.1111111111111p-4",
+    "0x1.e1e1e1e1e1e1ep-5", "0x1.af286bca1af28p-5", "0x1.8618618618618p-5"))
+SIN_SERIES = tuple(float.fromhex(h) for h in (
+    "0x1.0000000000000p+0", "-0x1.5555555555555p-3", "0x1.1111111111111p-7", "-0x1.a01a01a01a01ap-13",
+    "0x1.71de3a556c734p-19", "-0x1.ae64567f544e4p-26", "0x1.6124613a86d09p-33", "-0x1.ae7f3e733b81fp-41",
+    "0x1.952c77030ad4ap-49"))
+COS_SERIES = tuple(float.fromhex(h) for h in (
+    "0x1.0000000000000p+0", "-0x1.0000000000000p-1", "0x1.5555555555555p-5", "-0x1.6c16c16c16c17p-10",
+    "0x1.a01a01a01a01ap-16", "-0x1.27e4fb7789f5cp-22", "0x1.1eed8eff8d898p-29", "-0x1.93974a8c07c9dp-37",
+    "0x1.ae7f3e733b81fp-45", "-0x1.6827863b97d97p-53"))
+LN2 = float.fromhex("0x1.62e42fefa39efp-1")
+TWO_PI = float.fromhex("0x1.921fb54442d18p+2")
+SQRT_HALF = float.fromhex("0x1.6a09e667f3bcdp-1")
+
+
+def _horner(coef: tuple, t: np.ndarray) -> np.ndarray:
+    """sum coef[k] t^k, highest term first, one rounding per multiply and add."""
+    p = np.full_like(t, coef[-1])
+    for c in coef[-2::-1]:
+        np.multiply(p, t, out=p)
+        np.add(p, c, out=p)
+    return p
+
+
+def portable_ln(k: np.ndarray) -> np.ndarray:
+    """ln(k * 2^-53) for integers 1 <= k <= 2^53 (uint64). k = f * 2^b with
+    f in [sqrt(1/2), sqrt(2)) (exact), ln = (b - 53) ln 2 + 2 atanh(s),
+    s = (f - 1) / (f + 1), atanh by its series in s^2 (|s| <= 0.1716, 11
+    terms, truncation below 2^-56)."""
+    f, b = np.frexp(k.astype(np.float64))
+    e = b.astype(np.float64) - 53.0
+    low = f < SQRT_HALF
+    f[low] *= 2.0
+    e[low] -= 1.0
+    s = (f - 1.0) / (f + 1.0)
+    p = _horner(LN_SERIES, s * s)
+    return e * LN2 + (2.0 * s) * p
+
+
+def portable_cos_turns(k: np.ndarray) -> np.ndarray:
+    """cos(2 pi k 2^-53) for integers 0 <= k < 2^53 (uint64). The octant
+    q = k >> 50 and the offset r in [0, 1/8) turn are exact; odd octants
+    use 1/8 - r, so the series argument x = 2 pi w stays in [0, pi/4]; the
+    octant picks sin or cos of x and the sign."""
+    q = (k >> np.uint64(50)).astype(np.int64)
+    r = (k & np.uint64((1 << 50) - 1)).astype(np.float64) * (2.0 ** -53)
+    odd = (q & 1) == 1
+    r[odd] = 0.125 - r[odd]
+    x = TWO_PI * r
+    x2 = x * x
+    use_cos = (q == 0) | (q == 3) | (q == 4) | (q == 7)
+    v = np.empty_like(x)
+    v[use_cos] = _horner(COS_SERIES, x2[use_cos])
+    sn = ~use_cos
+    v[sn] = x[sn] * _horner(SIN_SERIES, x2[sn])
+    neg = (q >= 2) & (q <= 5)
+    v[neg] = -v[neg]
+    return v
+
+
+def _normal_chunk(seed: int, lo: int, m: int, mean: float, std: float) -> np.ndarray:
+    d = splitmix64(seed, 2 * m, start=2 * lo)
+    k1 = (d[0::2] >> np.uint64(11)) + np.uint64(1)
+    k2 = d[1::2] >> np.uint64(11)
+    z = np.sqrt(-2.0 * portable_ln(k1)) * portable_cos_turns(k2)
+    return (mean + std * z).astype(np.float32)
+
+
+def normal_f32(seed: int, n: int, mean: float = 0.0, std: float = 1.0, chunk: int = 1 << 21) -> np.ndarray:
+    """n normal draws (module docstring), chunks evaluated on a thread pool
+    (numpy releases the GIL inside its loops)."""
+    mean = float(np.float32(mean))
+    std = float(np.float32(std))
     out = np.empty(n, dtype=np.float32)
-    for lo in range(0, n, chunk):
+    starts = list(range(0, n, chunk))
+
+    def one(lo: int) -> None:
         m = min(chunk, n - lo)
-        d = splitmix64(seed, 2 * m, start=2 * lo)
-        u1 = ((d[0::2] >> np.uint64(11)).astype(np.float64) + 1.0) * (2.0 ** -53)
-        u2 = (d[1::2] >> np.uint64(11)).astype(np.float64) * (2.0 ** -53)
-        z = np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * math.pi * u2)
-        out[lo:lo + m] = (mean + std * z).astype(np.float32)
+        out[lo:lo + m] = _normal_chunk(seed, lo, m, mean, std)
+
+    if len(starts) <= 1:
+        for lo in starts:
+            one(lo)
+    else:
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(max_workers=min(len(starts), os.cpu_count() or 1)) as ex:
+            list(ex.map(one, starts))
     return out
 
 

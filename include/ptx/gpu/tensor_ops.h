@@ -265,14 +265,18 @@ void ptx_tensor_layer_norm_rows_f32(float* in, float* out, const float* gamma, c
  * intents, for callers that cannot allocate device memory at that moment
  * (allocator callbacks, processes whose cudaMalloc is routed into the pool
  * being managed, processes that reserved all device memory up front). The
- * scratch is a fixed device array inside this library (held by every GPU
- * that loads it until exit); the call allocates nothing.
+ * scratch is a fixed 256 KiB device array inside this library; the call
+ * allocates nothing.
  *   - n <= PTX_REDUCE_NOALLOC_MAX_ELEMENTS, else cudaErrorInvalidValue and no
  *     launch;
  *   - calls share the scratch: calls that overlap on the GPU race, so
  *     serialise them;
- *   - the first call on a device resolves the scratch address; make it
- *     before any stream capture begins. */
+ *   - the first call in a device's context loads the array and the kernels
+ *     (device memory, taken then and held until the context is destroyed)
+ *     and resolves the scratch address: make that first call (a warm-up call
+ *     will do) before reserving the rest of the device's memory, and before
+ *     any stream capture begins. After cudaDeviceReset the next call repeats
+ *     that set-up. */
 #define PTX_REDUCE_NOALLOC_MAX_ELEMENTS 33554432u
 cudaError_t ptx_tensor_reduce_f32_noalloc(const float* in, float* out, size_t n, int is_max, cudaStream_t stream);
 

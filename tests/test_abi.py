@@ -19,7 +19,20 @@ HEADERS = {
     "libptx_kernels.so": ["include/ptx/gpu/tensor_ops.h", "include/fercuda/b200/native.h"],
     "libptx_hook.so": ["include/ptx/ptx_hook.h"],
 }
-REFERENCE = Path("/root/reference")
+
+
+def _reference_dir() -> Path:
+    """$FERCUDA_REFERENCE_DIR, else oracle/Makefile's default (absent on a GPU box)."""
+    import os
+
+    env = os.environ.get("FERCUDA_REFERENCE_DIR")
+    if env:
+        return Path(env)
+    out = subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "print-ref"], capture_output=True, text=True)
+    return Path(out.stdout.strip() or "/nonexistent")
+
+
+REFERENCE = _reference_dir()
 
 
 def declared(header: Path) -> list[str]:

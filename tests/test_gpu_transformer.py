@@ -1,6 +1,8 @@
 """Decoder-only transformer forward (fer_transformer_forward) against the
-numpy oracle (oracle/transformer_ref.py, which rounds to bf16 at the same
-points as the GPU path), plus the properties batch sharding relies on:
+libtorch-CPU fixture of the benchmark model (tests/golden/, the reference's
+block op for op in float32) and against the numpy oracle
+(oracle/transformer_ref.py, which rounds to bf16 at the same points as the
+GPU path), plus the properties batch sharding relies on:
 sequences are independent, so any split of the batch gives bit-identical
 logits, and runs are bit-identical.
 
@@ -16,6 +18,7 @@ import numpy as np
 import pytest
 
 from fercuda_b200 import capi, synth
+from tests import fixture_check
 
 pytestmark = pytest.mark.gpu
 
@@ -185,3 +188,50 @@ def test_forward_bit_identical_over_ten_runs(session):
     session.free(bt)
     session.free(bl)
     m.close()
+
+
+def test_device_weight_fill_matches_host_generator(session):
+    """The device fill (fer_fill_normal_bf16) gives the host generator's bits
+    (synth.normal_bf16), element for element, at the transformer's and the
+    GEMM benchmark's standard deviations."""
+    import ctypes as C
+
+    import torch
+
+    for seed, std, n in ((4, 0.02, 5_000_003), (3, 1.0 / np.sqrt(8192), 1_048_577), (9, 1.0, 4099)):
+        dev = torch.empty(n, dtype=torch.int16, device="cuda")
+        rc = capi.kernels().fer_fill_normal_bf16(C.c_void_p(dev.data_ptr()), n, seed, C.c_float(std), None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        got = dev.cpu().numpy().view(np.uint16)
+        want = synth.normal_bf16(seed, n, 0.0, std)
+        assert np.array_equal(got, want), (seed, int((got != want).sum()))
+
+
+def test_benchmark_batch_vs_libtorch_fixture():
+    """The benchmark forward at its full size (B = 64 sequences of 512 tokens,
+    8 layers, d 1024, 16 heads, FFN 4096, vocab 32000) against logits that
+    PyTorch computed on the CPU in float32 for sequences 0, 21, 42 and 63
+    (tests/golden/transformer_b64_fixture.npz). The device weights are the
+    fixture's (same sha256); every digest holds the 2e-2 logits tolerance."""
+    import hashlib
+
+    cfg = synth.TRANSFORMER
+    L, d, h, F, V, S, B = cfg["layers"], cfg["d_model"], cfg["heads"], cfg["ffn"], cfg["vocab"], cfg["seq"], cfg["batch"]
+    fx = fixture_check.load()
+    seqs = fx["meta"]["seqs"]
+    with capi.Session(0, pool_bytes=6 << 30) as s:
+        m = capi.Transformer(s, L, d, h, F, V, B * S)
+        m.init_weights(cfg["weight_seed"], 0.02)
+        w = weights(s, m, m.weight_elements())
+        assert hashlib.sha256(w.astype("<u2").tobytes()).hexdigest() == fx["weights_sha256"]
+        toks = tokens_for(B, S, V, cfg["token_seed"])
+        assert np.array_equal(toks[seqs], fx["tokens"])
+        y = run(s, m, toks, V)
+        mine = y[seqs].cpu().numpy()
+        del y
+        assert np.isfinite(mine).all()
+        e = fixture_check.check(fx, mine, REQUIRED_TOL)
+        assert e["rows"] <= TIGHT_DEEP, e
+        print("vs libtorch fixture:", e)
+        m.close()

@@ -9,6 +9,11 @@ second smaller than the first so stale partials from the first call would
 show. The tolerance is the one the intent tests use for this reduction:
 bit-exact, since both paths run the same fixed-order kernels.
 
+A third test checks the property the entry point exists for: after the first
+call in the context (which loads its module), further calls leave the
+session pool's allocation count and bytes, torch's allocator and the
+driver's free-memory count unchanged.
+
 Collected last (file name) so a run that stops at its first failure has run
 everything else first; it passes alone in a fresh process too."""
 import ctypes as C
@@ -76,5 +81,35 @@ def test_noalloc_rejects_sizes_beyond_the_maximum(session):
     rc = capi.kernels().ptx_tensor_reduce_f32_noalloc(C.c_void_p(session.ptr_of(bx)), C.c_void_p(session.ptr_of(bo)),
                                                       MAX_ELEMENTS + 1, 0, C.c_void_p(session.stream()))
     assert rc == CUDA_ERROR_INVALID_VALUE
+    session.free(bx)
+    session.free(bo)
+
+
+def pool_stats(session):
+    st = capi.fer_pool_stats_t()
+    capi.check("fer_pool_get_stats", session.call("fer_pool_get_stats", C.byref(st)))
+    return (st.allocated_bytes, st.total_allocations, st.total_frees, st.allocated_blocks)
+
+
+def test_noalloc_calls_allocate_nothing(session):
+    import torch
+
+    n = 2_000_003
+    x = synth.normal_f32(80, n)
+    bx = session.alloc(capi.FER_DTYPE_F32, [n])
+    bo = session.alloc(capi.FER_DTYPE_F32, [1])
+    session.upload(bx, x)
+    args = (C.c_void_p(session.ptr_of(bx)), C.c_void_p(session.ptr_of(bo)), n, 0, C.c_void_p(session.stream()))
+    assert capi.kernels().ptx_tensor_reduce_f32_noalloc(*args) == 0      # set-up call
+    torch.cuda.synchronize()
+    before = (pool_stats(session), torch.cuda.memory_allocated(), torch.cuda.memory_reserved(),
+              torch.cuda.mem_get_info()[0])
+    for is_max in (0, 1, 0, 1):
+        a = args[:3] + (is_max,) + args[4:]
+        assert capi.kernels().ptx_tensor_reduce_f32_noalloc(*a) == 0
+    torch.cuda.synchronize()
+    after = (pool_stats(session), torch.cuda.memory_allocated(), torch.cuda.memory_reserved(),
+             torch.cuda.mem_get_info()[0])
+    assert after == before
     session.free(bx)
     session.free(bo)
