@@ -72,7 +72,7 @@ def profiled_traffic(name: str):
 
 def host_threads() -> int:
     try:
-        return len(os.sched_getaffinity(0))
+        return len(_ORIG_AFFINITY) or len(os.sched_getaffinity(0))
     except AttributeError:
         return os.cpu_count() or 1
 
@@ -397,11 +397,18 @@ class Transformer:
         self.model = capi.Transformer(s, L, d, h, F, V, T, cfg["eps"])
         if rank == 0:
             self.model.init_weights(cfg["weight_seed"], 0.02)
+        else:
+            # other weights until the broadcast arrives, so equal logits
+            # digests across GPU counts show that it did
+            self.model.init_weights(0x5EED0000 + rank, 0.02)
+        self.broadcast_bytes = 0
         if world > 1:
-            self._broadcast_weights(dist, torch)
+            self._broadcast_weights(dist)
         u = synth.uniform01(cfg["token_seed"], B * S)
         toks = np.minimum((u * V).astype(np.int32), V - 1).reshape(B, S)
-        self.toks = sharding.shard_tokens(toks, world, rank)
+        first, count = capi.transformer_shard(B, world, rank)
+        self.first_seq = first
+        self.toks = np.ascontiguousarray(toks[first:first + count])
         self.bt = s.alloc(capi.FER_DTYPE_I32, [self.B_local, S])
         self.bl = s.alloc(capi.FER_DTYPE_F32, [self.B_local, S, V])
         s.upload(self.bt, self.toks)
@@ -410,13 +417,18 @@ class Transformer:
         self.h2d = 4 * T
         self.d2h = 4 * T * V
 
-    def _broadcast_weights(self, dist, torch):
-        """Rank 0's weights reach every rank once, over NCCL (NVLink/NVSwitch)."""
-        ptr = self.s.ptr_of(self.model.weight_buffer())
-        t = sharding.device_bytes_as_tensor(torch, ptr, 2 * self.model.weight_elements())
-        torch.cuda.synchronize()
-        self.broadcast_bytes = sharding.broadcast_from_rank0(dist, t)
-        torch.cuda.synchronize()
+    def _broadcast_weights(self, dist):
+        """Rank 0's weights reach every rank once: fer_transformer_broadcast_weights,
+        one NCCL broadcast over NVLink/NVSwitch on a communicator the session
+        owns (fer_comm_init), released right after (no per-step collective)."""
+        uid = sharding.share_unique_id(dist, self.capi.comm_unique_id() if self.rank == 0 else None)
+        self.s.comm_init(uid, self.rank, self.world, 120_000)
+        self.broadcast_bytes = self.model.broadcast_weights(0)
+        self.s.comm_destroy()
+
+    def digests(self):
+        """Per-sequence digests of this rank's logits (fer_buffer_row_digests)."""
+        return self.s.row_digests(self.bl, 4 * self.S * self.V, self.B_local)
 
     def step(self, i):
         self.model.forward(self.bt, self.bl)
@@ -447,19 +459,32 @@ class Transformer:
         self.step(0)
         self.s.download(self.bl, self.hl)
 
-    def roofline_from_profile(self, prof):
+    def roofline_from_profile(self, prof, ms_per_step):
+        """GEMM roofline of the timed steps: each kernel class's share of a
+        forward comes from the event-instrumented pass (fer_transformer_profile),
+        its time from the timed region (share x ms_per_step), so
+        achieved = GEMM FLOPs per forward / (share x ms_per_step) follows
+        from the line's own ms_per_step."""
         pk, src = peak("bf16_tflops")
-        ach = prof.gemm_flops / (prof.gemm_ms * 1e-3) / 1e12
-        per_launch = prof.gemm_flops / max(1, prof.forwards) / (4 * self.cfg["layers"] + 1)   # mean over the GEMMs
+        fw = max(1, prof.forwards)
+        total = prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms
+        share = {k: getattr(prof, k) / total for k in ("gemm_ms", "attn_ms", "norm_ms", "other_ms")}
+        gemm_flops = prof.gemm_flops / fw
+        attn_flops = prof.attn_flops / fw
+        ach = gemm_flops / (share["gemm_ms"] * ms_per_step * 1e-3) / 1e12
+        per_launch = gemm_flops / (4 * self.cfg["layers"] + 1)   # mean over the GEMMs of a forward
         return {"bound": "tensor", "achieved": round(ach, 1), "peak": pk, "unit": "TFLOP/s",
                 "frac": round(ach / pk, 4), "traffic": profiled_traffic(self.kernel),
                 "traffic_note": "ncu DRAM bytes per GEMM launch, mean over the 33 GEMMs of a B=8 forward",
-                "algorithmic_flops_per_launch": round(per_launch), "peak_source": src + " (burst)",
-                "kernel": "gemm_bf16_tc2_kernel (all GEMMs of the forward)",
-                "share_of_forward": round(prof.gemm_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4),
-                "attention_tflops": round(prof.attn_flops / (prof.attn_ms * 1e-3) / 1e12, 1) if prof.attn_ms else None,
-                "attention_share": round(prof.attn_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4),
-                "norm_share": round(prof.norm_ms / (prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms), 4)}
+                "algorithmic_flops_per_launch": round(per_launch), "gemm_flops_per_forward": round(gemm_flops),
+                "peak_source": src + " (burst)", "kernel": "gemm_bf16_tc2_kernel (all GEMMs of the forward)",
+                "share_of_forward": round(share["gemm_ms"], 4),
+                "attention_tflops": round(attn_flops / (share["attn_ms"] * ms_per_step * 1e-3) / 1e12, 1)
+                if prof.attn_ms else None,
+                "attention_share": round(share["attn_ms"], 4), "norm_share": round(share["norm_ms"], 4),
+                "forward_tflops": round((gemm_flops + attn_flops) / (ms_per_step * 1e-3) / 1e12, 1),
+                "how": "shares from the event pass x the timed ms_per_step",
+                "event_pass_ms_per_forward": round(total / fw, 4)}
 
     @staticmethod
     def cpu(threads, seqs=1):
@@ -624,6 +649,37 @@ def timed_steps(wl, torch, stream, steps, warmup, dist, world):
     return t0.elapsed_time(t1)
 
 
+_ORIG_AFFINITY = set(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else set()
+
+
+def unbind() -> None:
+    """Back to every host thread the process started with (CPU baselines)."""
+    if _ORIG_AFFINITY:
+        os.sched_setaffinity(0, _ORIG_AFFINITY)
+
+
+def bind_to_gpu_numa_node(torch, local: int) -> dict:
+    """Pins this process to the host CPUs of its GPU's NUMA node (from sysfs)
+    before any pinned host buffer is made, so those buffers are first touched,
+    and therefore placed, in memory local to the GPU's PCIe root: the e2e
+    download of the logits then does not cross the socket interconnect."""
+    try:
+        p = torch.cuda.get_device_properties(local)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        dev = Path("/sys/bus/pci/devices") / bus
+        node = int((dev / "numa_node").read_text().strip())
+        cpus = set()
+        for part in (dev / "local_cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= _ORIG_AFFINITY
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return {"pci": bus, "numa_node": node, "cpus": len(cpus)}
+    except (OSError, ValueError, AttributeError) as e:
+        return {"error": str(e)[:80]}
+
+
 def max_over_ranks(v, torch, dist, world):
     return sharding.max_over_ranks(torch, dist, v, "cuda")
 
@@ -657,10 +713,34 @@ def subresults(s, capi, synth, torch, stream):
                 s.free(by)
     out["decode"] = decode_steps(s, capi, synth, torch)
     out["alloc_hook"] = hook_alloc_pairs(capi)
-    tl = Tlsf(s, capi, synth).run(ops=100_000)
+    tl = Tlsf(s, capi, synth).run()
     out["tlsf"] = {"metric": Tlsf.metric, "value": tl["tlsf"]["alloc_p50_ns"], "unit": "ns", "results": tl,
-                   "sample": "first 100k ops of the 1M-op trace (full trace: --workload tlsf)",
-                   "reference_tlsf_host": Tlsf.cpu_reference(ops=100_000)}
+                   "sample": "the full 1M-op trace (cudaMalloc: its first 50k ops)",
+                   "reference_tlsf_host": Tlsf.cpu_reference()}
+    return out
+
+
+def compact(sub: dict) -> dict:
+    """The figures of each subresult that the one-line summary keeps (the
+    full records go to stderr): value, unit, roofline achieved / peak / frac,
+    the CPU baseline's value, and the TLSF and allocator latencies."""
+    out = {}
+    for name, r in sub.items():
+        c = {"value": r.get("value"), "unit": r.get("unit")}
+        roof = r.get("roofline")
+        if roof:
+            c.update(achieved=roof.get("achieved"), peak=roof.get("peak"), frac=roof.get("frac"))
+        if r.get("cpu_baseline"):
+            c["cpu"] = r["cpu_baseline"]["value"]
+        if name == "tlsf":
+            t, cm = r["results"]["tlsf"], r["results"]["cudaMalloc"]
+            c.update(ops=t["ops"], alloc_p99_ns=t["alloc_p99_ns"], free_p50_ns=t["free_p50_ns"],
+                     cudaMalloc_p50_ns=cm["alloc_p50_ns"])
+        if name == "alloc_hook":
+            c["speedup_vs_cudamalloc"] = r.get("speedup_vs_cudamalloc")
+        if "bit_identical_rerun" in r:
+            c["bit_identical_rerun"] = r["bit_identical_rerun"]
+        out[name] = c
     return out
 
 
@@ -796,6 +876,12 @@ def run_reference(args, rank):
     emit(line)
 
 
+def cls_name_binds(workload: str) -> bool:
+    """Workloads whose e2e leg moves host buffers (every one but the
+    host-latency ones) run bound to their GPU's NUMA node."""
+    return workload not in ("tlsf", "decode")
+
+
 def emit(line: dict) -> None:
     """The result line goes to the process's original stdout; everything the
     native libraries print goes to stderr (fd 1 is redirected in main)."""
@@ -835,6 +921,7 @@ def main():
     import torch.distributed as dist
 
     torch.cuda.set_device(local)
+    numa = bind_to_gpu_numa_node(torch, local) if cls_name_binds(args.workload) else None
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
 
@@ -921,13 +1008,54 @@ def main():
     e0 = time.perf_counter()
     for _ in range(e2e_steps):
         wl.e2e_step()
-    e2e_s = max_over_ranks(time.perf_counter() - e0, torch, dist, world)
+    e2e_rank_s = time.perf_counter() - e0
+    e2e_s = max_over_ranks(e2e_rank_s, torch, dist, world)
+    # this rank's host<->device rate over the e2e steps (compute included)
+    d2h_gbs = wl.d2h * e2e_steps / e2e_rank_s / 1e9
+    d2h_all = [d2h_gbs]
+    if world > 1:
+        d2h_all = [None] * world
+        dist.all_gather_object(d2h_all, round(d2h_gbs, 2))
+
+    digest = None
+    if cls is Transformer:
+        # per-sequence digests of the logits of the last timed forward,
+        # gathered in sequence order: equal across GPU counts bit for bit
+        mine = wl.digests()
+        if world > 1:
+            parts = [None] * world
+            dist.all_gather_object(parts, (wl.first_seq, mine))
+        else:
+            parts = [(wl.first_seq, mine)]
+        seqs = [d for _, ds in sorted(parts) for d in ds]
+        print(json.dumps({"rank": rank, "first_sequence": wl.first_seq,
+                          "logits_digests": [f"{d:016x}" for d in mine]}), file=sys.stderr)
+        import hashlib
+
+        digest = {"sequences": len(seqs),
+                  "all": hashlib.sha256(np.array(seqs, np.uint64).tobytes()).hexdigest()[:16],
+                  "seq0": f"{seqs[0]:016x}", "seq63": f"{seqs[-1]:016x}"}
+
+    # steady state: a longer untimed run (>= 200 steps, >= 1 s) with its own
+    # clock samples, beside the K timed steps of the contract
+    steady = None
+    if cls is Transformer:
+        n_steady = max(200, int(1000.0 / max(1e-3, elapsed / args.steps)))
+        clocks2 = ClockSampler(local)
+        clocks2.start()
+        time.sleep(0.25)
+        clocks2.mark(True)
+        el2 = timed_steps(wl, torch, stream, n_steady, 0, dist, world)
+        clocks2.mark(False)
+        el2 = max_over_ranks(el2, torch, dist, world)
+        steady = {"steps": n_steady, "ms_per_step": round(el2 / n_steady, 5),
+                  "tokens_per_s": round(wl.global_tokens * n_steady / (el2 * 1e-3), 1), "clocks": clocks2.stop()}
 
     if rank == 0:
         if cls is Transformer:
             value = wl.global_tokens * args.steps / (elapsed * 1e-3)
             e2e_v = wl.global_tokens * e2e_steps / e2e_s
-            roof = wl.roofline_from_profile(prof)
+            roof = wl.roofline_from_profile(prof, elapsed / args.steps)
             launches = int(round(prof.launches / max(1, prof.forwards))) * args.steps
             unit_scale = 1.0
         else:
@@ -938,6 +1066,7 @@ def main():
             launches = wl.launches_per_step * args.steps
         cpu_base = None
         if world == 1:
+            unbind()
             cv, sample, cores = cls.cpu(host_threads())
             cpu_base = {"value": round(cv, 4), "unit": cls.unit, "cores": cores, "kind": "port",
                         "sample": sample + " (oracle/, restatement of the reference's path)"}
@@ -948,17 +1077,23 @@ def main():
                 "config": wl.config(world),
                 "e2e": {"value": round(e2e_v, 3), "unit": cls.unit, "h2d_bytes_per_step": wl.h2d * world,
                         "d2h_bytes_per_step": wl.d2h * world, "steps": e2e_steps,
-                        "api": "fer_upload_bytes + submit + fer_download_bytes (pinned host buffers)"},
+                        "api": "fer_upload_bytes + submit + fer_download_bytes (pinned host buffers)",
+                        "d2h_gbs_per_rank": [round(x, 2) for x in d2h_all], "numa": numa},
                 "roofline": roof, "cpu_baseline": cpu_base, "clocks": clk, "gpu_launches": launches,
                 "device_error_bits": errs}
         if cls is Transformer:
-            line["weight_broadcast_bytes"] = getattr(wl, "broadcast_bytes", 0)
+            line["weight_broadcast_bytes"] = wl.broadcast_bytes
+            line["weight_broadcast"] = "fer_transformer_broadcast_weights (NCCL, C++)" if world > 1 else "none (1 GPU)"
+            line["logits_digest"] = digest
+            line["steady"] = steady
             line["profile_ms_per_forward"] = {k: round(getattr(prof, k) / max(1, prof.forwards), 4)
                                               for k in ("gemm_ms", "attn_ms", "norm_ms", "other_ms")}
         if world == 1 and cls is Transformer and not args.no_subresults:
             wl.model.close()
             s.free(wl.bl)
-            line["subresults"] = subresults(s, capi, synth, torch, stream)
+            full = subresults(s, capi, synth, torch, stream)
+            print(json.dumps({"subresults": full}), file=sys.stderr)
+            line["subresults"] = compact(full)
         emit(line)
     if world > 1:
         dist.barrier()

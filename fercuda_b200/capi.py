@@ -289,6 +289,12 @@ CAPI_PROTOTYPES = {
     "fer_pool_get_stats": (S, [P, C.POINTER(fer_pool_stats_t)]),
     "fer_pool_alloc_raw": (S, [P, u64, C.POINTER(P)]),
     "fer_pool_free_raw": (S, [P, P]),
+    "fer_comm_unique_id": (S, [pu8]),
+    "fer_comm_init": (S, [P, pu8, C.c_int32, C.c_int32, u32]),
+    "fer_comm_destroy": (S, [P]),
+    "fer_transformer_broadcast_weights": (S, [P, u64, C.c_int32, pu64]),
+    "fer_transformer_shard": (S, [u32, C.c_int32, C.c_int32, pu32, pu32]),
+    "fer_buffer_row_digests": (S, [P, u64, u64, u32, pu64]),
 }
 
 CORE_PROTOTYPES = {
@@ -420,6 +426,24 @@ def desc(dtype: int, shape, immutable: bool = False, tag: int = 0) -> fer_buffer
     return d
 
 
+COMM_UNIQUE_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """fer_comm_unique_id: a fresh NCCL unique id (one rank makes it)."""
+    buf = (C.c_uint8 * COMM_UNIQUE_ID_BYTES)()
+    check("fer_comm_unique_id", capi().fer_comm_unique_id(buf))
+    return bytes(buf)
+
+
+def transformer_shard(global_batch: int, world: int, rank: int) -> tuple[int, int]:
+    """fer_transformer_shard: (first sequence, count) of rank's shard."""
+    first, count = C.c_uint32(), C.c_uint32()
+    check("fer_transformer_shard", capi().fer_transformer_shard(global_batch, world, rank, C.byref(first),
+                                                                C.byref(count)))
+    return first.value, count.value
+
+
 class Session:
     """Thin owner of a fer_session_t* with the calls the tests and the bench need."""
 
@@ -473,6 +497,18 @@ class Session:
         s = C.c_uint64()
         check("fer_get_session_stream", self.call("fer_get_session_stream", C.byref(s)))
         return s.value
+
+    def comm_init(self, uid: bytes, rank: int, world: int, timeout_ms: int = 0) -> None:
+        buf = (C.c_uint8 * COMM_UNIQUE_ID_BYTES).from_buffer_copy(uid)
+        check("fer_comm_init", self.call("fer_comm_init", buf, rank, world, timeout_ms))
+
+    def comm_destroy(self) -> None:
+        check("fer_comm_destroy", self.call("fer_comm_destroy"))
+
+    def row_digests(self, bid: int, row_bytes: int, rows: int) -> list[int]:
+        out = (C.c_uint64 * rows)()
+        check("fer_buffer_row_digests", self.call("fer_buffer_row_digests", bid, row_bytes, rows, out))
+        return list(out)
 
     def device_errors(self, clear: bool = True) -> int:
         v = C.c_uint32()
@@ -553,6 +589,14 @@ class Transformer:
         b = C.c_uint64()
         check("fer_transformer_weight_buffer", self.s.call("fer_transformer_weight_buffer", self.id, C.byref(b)))
         return b.value
+
+    def broadcast_weights(self, root: int = 0) -> int:
+        """fer_transformer_broadcast_weights over the session's communicator;
+        returns the bytes broadcast."""
+        n = C.c_uint64()
+        check("fer_transformer_broadcast_weights",
+              self.s.call("fer_transformer_broadcast_weights", self.id, root, C.byref(n)))
+        return n.value
 
     def forward(self, tokens: int, logits: int) -> int:
         job = C.c_uint64()

@@ -46,6 +46,10 @@ fer_status_t check_desc(const fer_buffer_desc_t& d, size_t* numel, size_t* bytes
 
 Session::~Session() {
     if (stream) cudaStreamSynchronize(stream);
+    if (comm) {
+        comm_release(comm);
+        comm = nullptr;
+    }
     models.clear();   // their workspace returns to the pool before it goes away
     for (auto& kv : jobs) {
         Job& j = kv.second;

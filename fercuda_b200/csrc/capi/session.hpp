@@ -83,6 +83,8 @@ struct CustomAlloc {
 
 class JitManager;
 struct Transformer;
+struct CommState;                 // NCCL communicator of a sharded session (comm.cpp)
+void comm_release(CommState* c);  // finalizes (bounded) or aborts, then frees
 
 struct Session {
     int device = 0;
@@ -128,6 +130,7 @@ struct Session {
     std::unique_ptr<JitManager> jit;
     std::unordered_map<uint64_t, std::shared_ptr<Transformer>> models;
     uint64_t next_model = 1;
+    CommState* comm = nullptr;
 
     ~Session();
 

@@ -1,10 +1,17 @@
 """Host-side plumbing of the batch-sharded transformer forward.
 
 One process per GPU. The global batch of sequences is split into equal,
-contiguous shards (rank r takes sequences [r*B/N, (r+1)*B/N)); the weights are
-made once on rank 0 and broadcast over the process group (NCCL over NVLink /
-NVSwitch on GPUs); no collective runs inside a forward, because sequences of
-a batch never interact. Step time is the maximum over ranks.
+contiguous shards (rank r takes sequences [r*B/N, (r+1)*B/N), the split of
+fer_transformer_shard); the weights are made once on rank 0 and copied into
+every rank's weight buffer by fer_transformer_broadcast_weights (one NCCL
+broadcast over NVLink / NVSwitch, in C++, on a communicator the session
+owns); no collective runs inside a forward, because sequences of a batch
+never interact. Step time is the maximum over ranks.
+
+What this module adds for Python callers: the shard arithmetic on numpy
+token arrays, handing the communicator's unique id from rank 0 to every rank
+over an existing torch.distributed group, and the max over ranks of a
+timing.
 
 The reference's multi-GPU weight copy is a serial peer copy from the source
 GPU to each destination (native/core/runtime/hot_multi_gpu_policy_main.inl:221-249,
@@ -31,21 +38,15 @@ def shard_tokens(tokens: np.ndarray, world: int, rank: int) -> np.ndarray:
     return np.ascontiguousarray(tokens[lo:hi])
 
 
-def device_bytes_as_tensor(torch, ptr: int, nbytes: int):
-    """A torch uint8 view of `nbytes` of device memory at `ptr` (no copy), so a
-    buffer of this library can take part in a torch.distributed collective."""
-
-    class _View:
-        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
-                                    "strides": None}
-
-    return torch.as_tensor(_View(), device="cuda")
-
-
-def broadcast_from_rank0(dist, tensor) -> int:
-    """Broadcasts `tensor` in place from rank 0; returns the bytes moved."""
-    dist.broadcast(tensor, src=0)
-    return tensor.numel() * tensor.element_size()
+def share_unique_id(dist, uid: bytes | None) -> bytes:
+    """Rank 0's communicator unique id (fer_comm_unique_id, 128 bytes) on
+    every rank of the torch.distributed group; other ranks pass None."""
+    box = [uid]
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.broadcast_object_list(box, src=0)
+    if not isinstance(box[0], (bytes, bytearray)) or len(box[0]) != 128:
+        raise RuntimeError("communicator unique id did not arrive")
+    return bytes(box[0])
 
 
 def max_over_ranks(torch, dist, value: float, device) -> float:

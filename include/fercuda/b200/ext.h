@@ -139,6 +139,47 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
                                      uint64_t* out_job_id);
 fer_status_t fer_transformer_destroy(fer_session_t* session, uint64_t model);
 
+/* ---- batch-sharded forward over the GPUs of one node ------------------------
+ * One process (or host thread) per GPU, each with its own session. The root
+ * rank makes the weights (fer_transformer_init_weights); one NCCL broadcast
+ * over NVLink / NVSwitch copies them into every rank's weight buffer in
+ * place; then each rank runs fer_transformer_forward on its contiguous shard
+ * of the global batch, with no collective inside a forward (sequences never
+ * interact, so the logits are bit-identical to a one-GPU forward of the
+ * whole batch). Replaces the reference's gpu_broadcast_tensor
+ * (native/core/runtime/modules/hot_multi_gpu_policy_main.inl:221-249), a
+ * serial cudaMemcpyPeer from the source GPU to each other GPU of one process.
+ *
+ * fer_comm_unique_id: on one rank; the caller hands the 128 bytes to every
+ * rank (any host channel). fer_comm_init: every rank, with the same id, its
+ * rank and the world size; binds an NCCL communicator to the session's
+ * device (released by fer_comm_destroy or fer_session_destroy). Waits are
+ * bounded by timeout_ms (0: 120 s): a rank that never joins, or a broadcast
+ * that does not finish, returns FER_STATUS_INTERNAL_ERROR (the communicator
+ * is aborted) instead of hanging. NCCL is opened at the first call
+ * (FERCUDA_NCCL_LIBRARY, else libnccl.so.2). */
+#define FER_COMM_UNIQUE_ID_BYTES 128
+fer_status_t fer_comm_unique_id(uint8_t* out_id);
+fer_status_t fer_comm_init(fer_session_t* session, const uint8_t* id, int32_t rank, int32_t world,
+                           uint32_t timeout_ms);
+fer_status_t fer_comm_destroy(fer_session_t* session);
+/* Broadcasts the model's weight buffer from `root` into every rank's, in
+ * place, ordered after the work queued on the session stream; returns when
+ * it has completed. Every rank calls it with the same root. */
+fer_status_t fer_transformer_broadcast_weights(fer_session_t* session, uint64_t model, int32_t root,
+                                               uint64_t* out_bytes);
+/* Rank's shard of a global batch: sequences [*out_first, *out_first +
+ * *out_count); the batch must split evenly. */
+fer_status_t fer_transformer_shard(uint32_t global_batch, int32_t world, int32_t rank, uint32_t* out_first,
+                                   uint32_t* out_count);
+/* 64-bit digest of each of `rows` consecutive rows of row_bytes bytes (a
+ * multiple of 16) of a buffer: the sum mod 2^64 of a mixing hash of every
+ * 16-byte chunk and its position within the row, so it depends only on the
+ * row's bytes (not on the row's index or the order of summation). Used to
+ * compare logits across ranks and GPU counts bit for bit. Synchronous. */
+fer_status_t fer_buffer_row_digests(fer_session_t* session, uint64_t buffer, uint64_t row_bytes, uint32_t rows,
+                                    uint64_t* out_digests);
+
 /* ---- KV cache and incremental decoding --------------------------------------
  * A KV cache of a model holds, per layer, the keys and values of up to
  * max_batch sequences x max_seq positions (bf16, [max_batch][heads][max_seq][64]

@@ -1,10 +1,14 @@
 """Batch sharding of the transformer forward, host side, on CPU.
 
-Two `gloo` ranks stand in for two GPUs: rank 0 makes the weights, broadcasts
-them, each rank runs the oracle forward on its shard of the global batch, and
-rank 0 checks the gathered logits against the whole-batch forward. The GPU
-path's own split-invariance (bit-identical logits for any split) is covered
-by the GPU tests; here the shard arithmetic and the collective steps are.
+Two `gloo` ranks stand in for two GPUs: rank 0 makes the weights and a
+communicator id, hands the id to the other rank (sharding.share_unique_id,
+as bench.py does before fer_comm_init), broadcasts the weights (a gloo
+broadcast stands in for fer_transformer_broadcast_weights, which is NCCL on
+the GPUs), each rank runs the oracle forward on its shard of the global
+batch, and rank 0 checks the gathered logits against the whole-batch forward.
+The GPU path's own split-invariance (bit-identical logits for any split) is
+covered by the GPU tests; here the shard arithmetic and the collective steps
+are.
 """
 from __future__ import annotations
 
@@ -62,8 +66,9 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         w = torch.zeros(2 * total, dtype=torch.uint8)        # the weight buffer as bytes, as on the GPUs
         if rank == 0:
             w.copy_(torch.from_numpy(synth.normal_bf16(4, total, 0.0, 0.02).view(np.uint8)))
-        moved = sharding.broadcast_from_rank0(dist, w)
-        assert moved == 2 * total
+        uid = sharding.share_unique_id(dist, bytes(range(128)) if rank == 0 else None)
+        assert uid == bytes(range(128))
+        dist.broadcast(w, src=0)
         wbits = w.numpy().view(np.uint16)
         u = synth.uniform01(5, c["batch"] * c["seq"])
         toks = np.minimum((u * c["vocab"]).astype(np.int32), c["vocab"] - 1).reshape(c["batch"], c["seq"])
@@ -97,3 +102,16 @@ def test_two_rank_broadcast_and_shard_forward():
     err, slowest = q.get(timeout=5)
     assert err <= 1e-6, err
     assert slowest == 2.0
+
+
+def test_c_abi_shard_matches_the_host_split():
+    from fercuda_b200 import capi
+
+    for world in (1, 2, 4, 8):
+        for r in range(world):
+            first, count = capi.transformer_shard(64, world, r)
+            assert (first, first + count) == sharding.shard_range(64, world, r)
+    with pytest.raises(capi.FerError):
+        capi.transformer_shard(64, 3, 0)
+    with pytest.raises(capi.FerError):
+        capi.transformer_shard(64, 2, 2)
