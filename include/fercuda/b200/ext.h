@@ -157,7 +157,9 @@ fer_status_t fer_transformer_destroy(fer_session_t* session, uint64_t model);
  * bounded by timeout_ms (0: 120 s): a rank that never joins, or a broadcast
  * that does not finish, returns FER_STATUS_INTERNAL_ERROR (the communicator
  * is aborted) instead of hanging. NCCL is opened at the first call
- * (FERCUDA_NCCL_LIBRARY, else libnccl.so.2). */
+ * (FERCUDA_NCCL_LIBRARY, else libnccl.so.2: the copy already loaded, if the
+ * process has one). A process that also loads another NCCL-linked library
+ * (PyTorch) should load that one first, so that one copy serves both. */
 #define FER_COMM_UNIQUE_ID_BYTES 128
 fer_status_t fer_comm_unique_id(uint8_t* out_id);
 fer_status_t fer_comm_init(fer_session_t* session, const uint8_t* id, int32_t rank, int32_t world,

@@ -16,6 +16,7 @@ import socket
 
 import numpy as np
 import pytest
+import torch  # noqa: F401  (first, so its libnccl.so.2 is the copy the library opens)
 
 from fercuda_b200 import capi, synth
 
