@@ -4,31 +4,26 @@
 // qkv: [B*S, 3*d] bf16 row-major (q | k | v; head h at columns h*64 of each
 // third); out: [B*S, d] bf16. S must be a multiple of 128.
 //
-// One CTA per (128-query tile, head, sequence), two CTAs per SM (97 KB of
-// shared memory and 256 tensor-memory columns each). Per key block j (64
+// One CTA per (128-query tile, head, sequence), three CTAs per SM (64 KB of
+// shared memory and 128 tensor-memory columns each). Per key block j (64
 // keys, j = 0 .. 2 * query tile + 1):
-//   warp 0      TMA: Q once ([128 rows x 64 bf16]), K_j and V_j into 3-deep
+//   warp 0      TMA: Q once ([128 rows x 64 bf16]), K_j and V_j into 2-deep
 //               rings ([64 rows x 64 bf16]), all 128-byte swizzled boxes
-//   warp 1      tcgen05.mma from one thread: S_j = Q K_j^T (M128 N64, f32)
-//               into one of two tensor-memory score buffers, two blocks ahead
-//               of the softmax; O += P_j V_j (M128 N64, K = 64 keys) once P_j
-//               is written, into one of two shared-memory P buffers
+//   warp 1      tcgen05.mma from one thread: S = Q K_j^T (M128 N64, f32 in
+//               tensor memory), issued for block j+1 as soon as the softmax
+//               threads have read block j's scores, then O += P_j V_j (M128
+//               N64, K = 64 keys) once P_j is written
 //   warps 2..5  one query row per thread: scores from tensor memory
-//               (tcgen05.ld), causal mask on the two diagonal blocks, the
-//               block's row max in the log2 domain, p = 2^(s*scale - m)
-//               (ex2.approx), row sum in f32, P rounded to bf16 into swizzled
-//               shared memory (the A operand of the P.V MMA).
-// The running max m a row subtracts is raised only when the block's max
-// exceeds it by more than 8 (log2 units, so p <= 256): softmax is invariant
-// to the constant subtracted, and the rescale of the row's O accumulator
-// (tcgen05.ld / st, after P_{j-1} V_j has landed) then happens a few times
-// per row instead of whenever the max grows. With two score buffers and two
-// P buffers the softmax of block j overlaps S_{j+1}, S_{j+2} and P_{j-1} V_{j-1}
-// on the tensor core; block j waits on the P.V chain only for P_{j-2} V_{j-2}
-// (its P buffer's last reader), and for P_{j-1} V_{j-1} when it rescales O.
-// Finally o / l is rounded to bf16 and stored. The arithmetic is the online
-// softmax of the mma.sync kernel in xfmr_kernels.cu and of the oracle's
-// exp(s - max) / sum, with P rounded to bf16 before P.V.
+//               (tcgen05.ld), causal mask on the two diagonal blocks, running
+//               max in the log2 domain, p = 2^(s*scale - m) (ex2.approx), row
+//               sum in f32, P rounded to bf16 into swizzled shared memory (the
+//               A operand of the P.V MMA). O accumulates in tensor memory
+//               across key blocks; when a row's max grows the softmax thread
+//               rescales its O row in place (tcgen05.ld / st) before the
+//               next P.V lands on it.
+// Finally o / l is rounded to bf16 and stored. The arithmetic is the same
+// online softmax as the mma.sync kernel in xfmr_kernels.cu (and the oracle's
+// exp(s - max) / sum with P rounded to bf16 before P.V).
 // Every wait is bounded (about one second): on timeout the kernel records an
 // error bit, stops, releases tensor memory and returns. No TMA multicast.
 #include "sm100_util.cuh"
@@ -46,22 +41,19 @@ using namespace fer::dev;
 
 constexpr int TQ = 128;                   // queries per CTA
 constexpr int TK = 64;                    // keys per block
-constexpr int KV_STAGES = 3;              // K and V ring depth
 constexpr int Q_BYTES = TQ * 128;         // [128 rows x 64 bf16], 16 KiB
 constexpr int KV_BYTES = TK * 128;        // [64 rows x 64 bf16], 8 KiB
 constexpr int P_BYTES = TQ * TK * 2;      // [128 rows x 64 keys bf16], 16 KiB
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = Q_BYTES;                          // KV_STAGES K buffers
-constexpr int OFF_V = OFF_K + KV_STAGES * KV_BYTES;     // KV_STAGES V buffers
-constexpr int OFF_P = OFF_V + KV_STAGES * KV_BYTES;     // two P buffers
-constexpr int SMEM_BYTES = OFF_P + 2 * P_BYTES + 1024;
+constexpr int OFF_K = Q_BYTES;            // two K buffers
+constexpr int OFF_V = OFF_K + 2 * KV_BYTES;   // two V buffers
+constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
+constexpr int SMEM_BYTES = OFF_P + P_BYTES + 1024;
 constexpr int kThreads = 192;
-constexpr int kCtasPerSm = 2;
-constexpr uint32_t TMEM_COLS = 256;       // S buffers at columns [0, 64) and [64, 128), O at [128, 192)
-constexpr uint32_t COL_O = 128;
-constexpr float kRescaleSlack = 8.0f;     // log2 units the running max may lag the block max
+constexpr int kCtasPerSm = 3;
+constexpr uint32_t TMEM_COLS = 128;       // S at columns [0, 64), O at [64, 128)
+constexpr uint32_t COL_O = 64;
 static_assert(kCtasPerSm * TMEM_COLS <= 512, "tensor memory per SM");
-static_assert(kCtasPerSm * SMEM_BYTES <= 227 * 1024, "shared memory per SM");
 
 // kind::f16 instruction descriptors: f32 accumulate, bf16 A and B, M = 128.
 // S = Q K^T: A and B K-major, N = 64. O = P V: A K-major, B (V) N-major, N = 64.
@@ -71,14 +63,14 @@ constexpr uint32_t kIdescPV =
 
 struct Bars {
     uint64_t q_full;
-    uint64_t k_full[KV_STAGES];
-    uint64_t k_empty[KV_STAGES];
-    uint64_t v_full[KV_STAGES];
-    uint64_t v_empty[KV_STAGES];
-    uint64_t s_full[2];
-    uint64_t s_free[2];
-    uint64_t p_full[2];
-    uint64_t o_full[2];      // P_j V_j complete, one barrier per P buffer (j & 1)
+    uint64_t k_full[2];
+    uint64_t k_empty[2];
+    uint64_t v_full[2];
+    uint64_t v_empty[2];
+    uint64_t s_full;
+    uint64_t s_free;
+    uint64_t p_full;
+    uint64_t o_full;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -195,19 +187,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
     if (threadIdx.x == 0) {
         mbar_init(&bars.q_full, 1);
-        for (int i = 0; i < KV_STAGES; ++i) {
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&bars.k_full[i], 1);
             mbar_init(&bars.k_empty[i], 1);
             mbar_init(&bars.v_full[i], 1);
             mbar_init(&bars.v_empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars.s_full[i], 1);
-            mbar_init(&bars.s_free[i], 4);
-            mbar_init(&bars.p_full[i], 4);
-        }
-        mbar_init(&bars.o_full[0], 1);
-        mbar_init(&bars.o_full[1], 1);
+        mbar_init(&bars.s_full, 1);
+        mbar_init(&bars.s_free, 4);
+        mbar_init(&bars.p_full, 4);
+        mbar_init(&bars.o_full, 1);
         bars.abort_flag = 0;
         fence_mbar_init();
     }
@@ -225,71 +214,73 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     volatile int* abort_flag = &bars.abort_flag;
 
     if (warp == 0) {
-        // ---------------- TMA producers: lane 0 loads Q once and then K_j,
-        // lane 1 loads V_j, each into ring slot j % 3 as soon as the slot's
-        // previous block has been consumed (S_{j-3} for K, P_{j-3} V_{j-3}
-        // for V); the two lanes wait independently.
+        // ---------------- TMA producer
         if (lane == 0) {
             mbar_arrive_expect_tx(&bars.q_full, Q_BYTES);
             tma_load_2d(sbase + OFF_Q, &tmq, h * 64, seq_row0 + qt * TQ, &bars.q_full);
         }
-        if (lane < 2) {
-            const bool is_k = lane == 0;
-            uint64_t* full = is_k ? bars.k_full : bars.v_full;
-            uint64_t* empty = is_k ? bars.k_empty : bars.v_empty;
-            const uint32_t off = is_k ? OFF_K : OFF_V;
-            const int col = (is_k ? d : 2 * d) + h * 64;
-            for (int j = 0; j < n_k && !*abort_flag; ++j) {
-                const int st = j % KV_STAGES;
-                const uint32_t use = static_cast<uint32_t>(j / KV_STAGES);
-                if (!mbar_wait(&empty[st], (use & 1u) ^ 1u)) {
-                    report(err, kErrTimeoutSync);
-                    *abort_flag = 1;
-                    break;
-                }
-                mbar_arrive_expect_tx(&full[st], KV_BYTES);
-                tma_load_2d(sbase + off + st * KV_BYTES, &tmkv, col, seq_row0 + j * TK, &full[st]);
-            }
-        }
         __syncwarp();
+        for (int j = 0; j < n_k && !warp_flag(abort_flag); ++j) {
+            const int st = j & 1;
+            const uint32_t use = static_cast<uint32_t>(j >> 1);
+            if (!warp_wait(&bars.k_empty[st], (use & 1u) ^ 1u)) {
+                if (lane == 0) report(err, kErrTimeoutSync);
+                *abort_flag = 1;
+                break;
+            }
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&bars.k_full[st], KV_BYTES);
+                tma_load_2d(sbase + OFF_K + st * KV_BYTES, &tmkv, d + h * 64, seq_row0 + j * TK, &bars.k_full[st]);
+            }
+            __syncwarp();
+            if (!warp_wait(&bars.v_empty[st], (use & 1u) ^ 1u)) {
+                if (lane == 0) report(err, kErrTimeoutSync);
+                *abort_flag = 1;
+                break;
+            }
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&bars.v_full[st], KV_BYTES);
+                tma_load_2d(sbase + OFF_V + st * KV_BYTES, &tmkv, 2 * d + h * 64, seq_row0 + j * TK,
+                            &bars.v_full[st]);
+            }
+            __syncwarp();
+        }
     } else if (warp == 1) {
-        // ---------------- MMA issuer. S_j goes into score buffer j & 1 once
-        // the softmax has read S_{j-2} from it; P_j V_j follows P_j. Order of
-        // issue: S_0, S_1, then per block S_{j+2} (as soon as the softmax has
-        // read S_j, so it runs under that softmax) and P_j V_j.
+        // ---------------- MMA issuer: S_{j+1} goes in as soon as the softmax
+        // threads have read S_j, so it runs under their exponentials; P_j V_j
+        // follows once P_j is written.
         auto issue_s = [&](int j) -> bool {
-            const int st = j % KV_STAGES, b = j & 1;
-            if (!warp_wait(&bars.k_full[st], static_cast<uint32_t>(j / KV_STAGES) & 1u)) return false;
-            if (j >= 2 && !warp_wait(&bars.s_free[b], static_cast<uint32_t>((j - 2) >> 1) & 1u)) return false;
+            const int st = j & 1;
+            if (!warp_wait(&bars.k_full[st], static_cast<uint32_t>(j >> 1) & 1u)) return false;
+            if (j > 0 && !warp_wait(&bars.s_free, static_cast<uint32_t>(j - 1) & 1u)) return false;
             fence_after();
             if (lane == 0) {
                 const uint32_t q = sbase + OFF_Q, k = sbase + OFF_K + st * KV_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    mma(tmem + b * 64, sdesc(q + kk * 32, 16, 1024), sdesc(k + kk * 32, 16, 1024), kIdescS,
-                        kk ? 1u : 0u);
+                    mma(tmem, sdesc(q + kk * 32, 16, 1024), sdesc(k + kk * 32, 16, 1024), kIdescS, kk ? 1u : 0u);
                 commit(&bars.k_empty[st]);
-                commit(&bars.s_full[b]);
+                commit(&bars.s_full);
             }
             __syncwarp();
             return true;
         };
-        bool ok = warp_wait(&bars.q_full, 0) && issue_s(0) && (n_k < 2 || issue_s(1));
+        bool ok = warp_wait(&bars.q_full, 0) && issue_s(0);
         for (int j = 0; j < n_k && ok && !warp_flag(abort_flag); ++j) {
-            const int st = j % KV_STAGES, b = j & 1;
-            if (j + 2 < n_k && !(ok = issue_s(j + 2))) break;
-            ok = warp_wait(&bars.p_full[b], static_cast<uint32_t>(j >> 1) & 1u) &&
-                 warp_wait(&bars.v_full[st], static_cast<uint32_t>(j / KV_STAGES) & 1u);
+            const uint32_t ph = static_cast<uint32_t>(j) & 1u;
+            if (j + 1 < n_k && !(ok = issue_s(j + 1))) break;
+            const int st = j & 1;
+            ok = warp_wait(&bars.p_full, ph) && warp_wait(&bars.v_full[st], static_cast<uint32_t>(j >> 1) & 1u);
             if (!ok) break;
             fence_after();
             if (lane == 0) {
-                const uint32_t p = sbase + OFF_P + b * P_BYTES, v = sbase + OFF_V + st * KV_BYTES;
+                const uint32_t p = sbase + OFF_P, v = sbase + OFF_V + st * KV_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < TK / 16; ++kk)
                     mma(tmem + COL_O, sdesc(p + kk * 32, 16, 1024), sdesc(v + kk * 2048, KV_BYTES, 1024), kIdescPV,
                         (j | kk) ? 1u : 0u);
                 commit(&bars.v_empty[st]);
-                commit(&bars.o_full[b]);
+                commit(&bars.o_full);
             }
             __syncwarp();
         }
@@ -305,17 +296,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         float m = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int j = 0; j < n_k; ++j) {
-            const int b = j & 1;
-            if (warp_flag(abort_flag) || !warp_wait(&bars.s_full[b], static_cast<uint32_t>(j >> 1) & 1u)) {
+            const uint32_t ph = static_cast<uint32_t>(j) & 1u;
+            if (warp_flag(abort_flag) || !warp_wait(&bars.s_full, ph)) {
                 ok = false;
                 break;
             }
             fence_after();
             float sv[TK];
-            tmem_ld64(trow + b * 64, sv);
+            tmem_ld64(trow, sv);
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars.s_free[b]);   // S_{j+2} may overwrite this buffer now
+            if (lane == 0) mbar_arrive(&bars.s_free);   // S_{j+1} may overwrite S now
             const int kb = j * TK - qt * TQ;            // first key of the block, relative to the tile's first query
             if (kb + TK - 1 > 0) {
 #pragma unroll
@@ -327,27 +318,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             for (int e = 0; e < 8; ++e) mx[e] = sv[e];
 #pragma unroll
             for (int e = 8; e < TK; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[e]);
-            const float bmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale_log2;
-            // raise the subtracted max only when the block's exceeds it by
-            // more than the slack (always on the first block with a key)
-            const bool raise = bmax > m + kRescaleSlack;
-            const float m_new = raise ? bmax : m;
-            const float alpha = raise ? ex2(m - m_new) : 1.0f;     // 0 while m is -inf
-            // P buffer b's last reader is P_{j-2} V_{j-2}; o_full[b] counts
-            // the P.V products on buffer b, and this warp has seen every
-            // earlier one, so the parity of that product is unambiguous
-            if (j >= 2) {
-                if (!warp_wait(&bars.o_full[b], static_cast<uint32_t>((j - 2) >> 1) & 1u)) {
-                    ok = false;
-                    break;
-                }
+            const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            const float m_new = fmaxf(m, smax * scale_log2);
+            const float alpha = ex2(m - m_new);
+            // P_{j-1} V_{j-1} done: P's buffer is free and O holds every
+            // earlier block
+            if (j > 0 && !warp_wait(&bars.o_full, ph ^ 1u)) {
+                ok = false;
+                break;
             }
-            // p = 2^(s*scale - m_new), row sum, P (bf16) into P buffer b
+            fence_after();
+            // p = 2^(s*scale - m_new), row sum, P (bf16) into shared memory
             float sm[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) sm[e] = 0.0f;
-            const uint32_t prow = sbase + OFF_P + b * P_BYTES + r * 128;
 #pragma unroll
             for (int c = 0; c < TK / 32; ++c) {
                 uint32_t w[16];
@@ -359,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                     sm[(e + 1) & 7] += p1;
                     w[e >> 1] = pack_bf16x2(p0, p1);
                 }
+                const uint32_t prow = sbase + OFF_P + r * 128;
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4) {
                     const int chunk = (c & 1) * 4 + q4;
@@ -367,23 +353,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 }
             }
             const float sum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
-            // a rescale of O waits for P_{j-1} V_{j-1} to be in it (P_j V_j is
-            // issued only after this warp's p_full below)
+            // O holds sum_{i<j} P_i V_i scaled by 2^-m: rescale it in place
+            // before P_j V_j accumulates on it.
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-                if (!warp_wait(&bars.o_full[b ^ 1], static_cast<uint32_t>((j - 1) >> 1) & 1u)) {
-                    ok = false;
-                    break;
-                }
-                fence_after();
-                {
 #pragma unroll 1
-                    for (int c = 0; c < 2; ++c) {
-                        float ov[32];
-                        tmem_ld32(trow + COL_O + c * 32, ov);
+                for (int c = 0; c < 2; ++c) {
+                    float ov[32];
+                    tmem_ld32(trow + COL_O + c * 32, ov);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-                        tmem_st32(trow + COL_O + c * 32, ov);
-                    }
+                    for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+                    tmem_st32(trow + COL_O + c * 32, ov);
                 }
             }
             l = l * alpha + sum;
@@ -391,9 +370,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             fence_proxy_async_smem();   // P is read by the tensor core (async proxy)
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars.p_full[b]);
+            if (lane == 0) mbar_arrive(&bars.p_full);
         }
-        if (ok && !warp_wait(&bars.o_full[(n_k - 1) & 1], static_cast<uint32_t>((n_k - 1) >> 1) & 1u)) ok = false;
+        if (ok && !warp_wait(&bars.o_full, static_cast<uint32_t>(n_k - 1) & 1u)) ok = false;
         if (!ok) {
             if (lane == 0) report(err, kErrTimeoutMma);
             *abort_flag = 1;
