@@ -641,7 +641,9 @@ def timed_steps(wl, torch, stream, steps, warmup, dist, world):
     if world > 1:
         dist.barrier()
     t0.record(stream)
+    h0 = time.perf_counter()
     run(warmup, steps)
+    wl.host_issue_s = time.perf_counter() - h0   # host time to issue the K steps
     t1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -695,7 +697,9 @@ def subresults(s, capi, synth, torch, stream):
         unit_scale = 1e9 if cls is not Gemm else 1e12
         out[name] = {"metric": cls.metric, "value": round(wl.units_per_step * steps / (el * 1e-3) / unit_scale, 2),
                      "unit": cls.unit, "steps": steps, "config": wl.config(1), "roofline": wl.roofline(med),
-                     "device_error_bits": s.device_errors()}
+                     "device_error_bits": s.device_errors(),
+                     "host_us_per_call": round(wl.host_issue_s / steps * 1e6, 3),
+                     "device_us_per_call": round(med * 1e3, 3)}
         cv, sample, cores = cls.cpu(host_threads())
         out[name]["cpu_baseline"] = {"value": round(cv, 6), "unit": cls.unit, "cores": cores, "kind": "port",
                                      "sample": sample + " (oracle/, restatement of the reference's path)"}
@@ -740,6 +744,8 @@ def compact(sub: dict) -> dict:
             c["speedup_vs_cudamalloc"] = r.get("speedup_vs_cudamalloc")
         if "bit_identical_rerun" in r:
             c["bit_identical_rerun"] = r["bit_identical_rerun"]
+        if name == "fused_elementwise":
+            c.update(host_us_per_call=r.get("host_us_per_call"), device_us_per_call=r.get("device_us_per_call"))
         out[name] = c
     return out
 
