@@ -26,6 +26,7 @@
 // exp(s - max) / sum with P rounded to bf16 before P.V).
 // Every wait is bounded (about one second): on timeout the kernel records an
 // error bit, stops, releases tensor memory and returns. No TMA multicast.
+#include "pdl.cuh"
 #include "sm100_util.cuh"
 #include "tmap.cuh"
 
@@ -34,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 namespace {
 
@@ -173,15 +175,31 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attn_causal_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
-                   __nv_bfloat16* __restrict__ out, int S, int d, float scale_log2, uint32_t* err) {
+                   __nv_bfloat16* __restrict__ out, int S, int d, int heads, int tile_major, float scale_log2,
+                   uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_addr(smem);
 
-    const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);   // longest tiles first
-    const int h = blockIdx.y;
-    const int seq_row0 = static_cast<int>(blockIdx.z) * S;
+    // Work item of this CTA (1-D grid). Head-major (the tiles of one head on
+    // consecutive CTAs, longest first, so they share K/V in L2), or, when the
+    // grid is under about two waves, tile-major (every head's longest tile in
+    // the first wave, the shortest ones last, so the tail is a short tile).
+    const int n_qt = S / TQ;
+    const int bid = static_cast<int>(blockIdx.x);
+    int qt, h, bseq;
+    if (tile_major) {
+        const int per = static_cast<int>(gridDim.x) / n_qt;     // heads * sequences
+        qt = n_qt - 1 - bid / per;
+        h = (bid % per) % heads;
+        bseq = (bid % per) / heads;
+    } else {
+        qt = n_qt - 1 - bid % n_qt;
+        h = (bid / n_qt) % heads;
+        bseq = (bid / n_qt) / heads;
+    }
+    const int seq_row0 = bseq * S;
     const int n_k = (qt + 1) * (TQ / TK);                                               // keys 0 .. end of tile
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -212,6 +230,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     fence_after();
     const uint32_t tmem = bars.tmem_base;
     volatile int* abort_flag = &bars.abort_flag;
+    // set-up above touches no global memory (overlaps the previous kernel
+    // under programmatic launch)
+    fer::dev::pdl_begin();
 
     if (warp == 0) {
         // ---------------- TMA producer
@@ -433,8 +454,28 @@ extern "C" cudaError_t fer_attn_causal_tc(const void* qkv, void* out, int B, int
         cudaFuncSetAttribute(attn_causal_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (attr_rc != cudaSuccess) return attr_rc;
     const float scale_log2 = 1.4426950408889634f / 8.0f;   // log2(e) / sqrt(64)
-    const dim3 grid(S / TQ, heads, B);
-    attn_causal_tc<<<grid, kThreads, SMEM_BYTES, stream>>>(tmq, tmkv, static_cast<__nv_bfloat16*>(out), S, d,
-                                                           scale_log2, err);
+    const long long ctas = static_cast<long long>(S / TQ) * heads * B;
+    if (ctas > 0x7fffffffll) return cudaErrorNotSupported;
+    static const int sms = [] {
+        int dev = 0, v = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
+    const int tile_major = ctas <= 2ll * kCtasPerSm * sms ? 1 : 0;
+    const dim3 grid(static_cast<unsigned>(ctas));
+    static const bool pdl = [] {   // as the GEMM: off with FERCUDA_GEMM_PDL=0 (launch_pdl honours FERCUDA_PDL)
+        const char* e = std::getenv("FERCUDA_GEMM_PDL");
+        return !(e && e[0] == '0');
+    }();
+    if (pdl) {
+        const cudaError_t e = fer::host::launch_pdl(attn_causal_tc, grid, dim3(kThreads), SMEM_BYTES, stream, tmq, tmkv,
+                                                    static_cast<__nv_bfloat16*>(out), S, d, heads, tile_major,
+                                                    scale_log2, err);
+        return e != cudaSuccess ? e : cudaGetLastError();
+    }
+    fer_pdl_note_launch();   // the kernel triggers its dependents under either launch
+    attn_causal_tc<<<grid, kThreads, SMEM_BYTES, stream>>>(tmq, tmkv, static_cast<__nv_bfloat16*>(out), S, d, heads,
+                                                           tile_major, scale_log2, err);
     return cudaGetLastError();
 }

@@ -700,6 +700,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = bars.tmem_base;
     volatile int* abort_flag = &bars.abort_flag;
+    // Set-up above touches no global memory: under programmatic launch it
+    // overlaps the previous kernel's tail. Every thread waits for that kernel
+    // here and then lets the next kernel be scheduled (no-ops under a plain
+    // launch).
+    fer::dev::pdl_begin();
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs): own A rows, own B columns
@@ -904,6 +909,17 @@ int sm_count() {
     return n;
 }
 
+// Programmatic launch of the 2-CTA kernel (its set-up overlaps the tail of
+// the kernel before; at 4096 tokens per GPU the forward takes 2-3% less
+// time, at 32768 the same): on unless FERCUDA_GEMM_PDL=0 or FERCUDA_PDL=0.
+bool tc2_pdl() {
+    static const bool on = [] {
+        const char* e = std::getenv("FERCUDA_GEMM_PDL");
+        return !(e && e[0] == '0') && fer::host::pdl_enabled();
+    }();
+    return on;
+}
+
 int g_gemm_mode = 0;        // 0: 2-CTA kernel where it applies, 1: always the 1-CTA kernel
 std::atomic<int> g_gemm_clusters{-1};   // co-resident 2-CTA clusters (queried once; same value from any thread)
 
@@ -965,8 +981,23 @@ cudaError_t gemm_ex(const void* a, const void* b, void* c, const float* resid, i
         if (clusters > 0) {
             const int tiles2 = ((M + 255) / 256) * ((N + BN - 1) / BN);
             const int ncl = tiles2 < clusters ? tiles2 : clusters;
-            gemm_bf16_tc2_kernel<<<2 * ncl, kThreads, SMEM2_BYTES, stream>>>(ma, mb, mc, M, N, K, epi,
-                                                                               gemm_group_m((N + BN - 1) / BN), err);
+            const int gm = gemm_group_m((N + BN - 1) / BN);
+            fer_pdl_note_launch();   // the kernel triggers its dependents under either launch
+            if (tc2_pdl()) {
+                cudaLaunchConfig_t cfg{};
+                cfg.gridDim = dim3(2 * ncl);
+                cfg.blockDim = dim3(kThreads);
+                cfg.dynamicSmemBytes = SMEM2_BYTES;
+                cfg.stream = stream;
+                cudaLaunchAttribute at[1];
+                at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+                at[0].val.programmaticStreamSerializationAllowed = 1;
+                cfg.attrs = at;
+                cfg.numAttrs = 1;
+                const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_tc2_kernel, ma, mb, mc, M, N, K, epi, gm, err);
+                return e != cudaSuccess ? e : cudaGetLastError();
+            }
+            gemm_bf16_tc2_kernel<<<2 * ncl, kThreads, SMEM2_BYTES, stream>>>(ma, mb, mc, M, N, K, epi, gm, err);
             return cudaGetLastError();
         }
     }
