@@ -45,7 +45,14 @@ fer_status_t check_desc(const fer_buffer_desc_t& d, size_t* numel, size_t* bytes
 }
 
 Session::~Session() {
-    if (stream) cudaStreamSynchronize(stream);
+    // The session's own stream is synchronised. A stream the caller attached
+    // (fer_set_session_stream) belongs to the caller, who may already have
+    // destroyed it (the reference's destructor never touches the stream):
+    // the device is synchronised instead.
+    if (stream) {
+        if (pool && stream == gpu_hot_get_stream(pool, 0)) cudaStreamSynchronize(stream);
+        else cudaDeviceSynchronize();
+    }
     if (comm) {
         comm_release(comm);
         comm = nullptr;
@@ -610,7 +617,11 @@ fer_status_t fer_download_f32(fer_session_t* session, uint64_t buffer_id, float*
 
 fer_status_t fer_set_session_stream(fer_session_t* session, uint64_t stream_handle) {
     FER_SESSION(session);
-    S.stream = reinterpret_cast<cudaStream_t>(static_cast<uintptr_t>(stream_handle));
+    const cudaStream_t next = reinterpret_cast<cudaStream_t>(static_cast<uintptr_t>(stream_handle));
+    // jobs still waiting for a shared completion event get it on the stream
+    // they ran on now, while that stream is certainly alive
+    if (next != S.stream) S.close_open();
+    S.stream = next;
     return ok();
 }
 
