@@ -465,7 +465,9 @@ class Transformer:
         its time from the timed region (share x ms_per_step), so
         achieved = GEMM FLOPs per forward / (share x ms_per_step) follows
         from the line's own ms_per_step."""
-        pk, src = peak("bf16_tflops")
+        # the GEMMs run inside a long, power-capped step (20+ forwards back to
+        # back), so the denominator is the sustained bf16 GEMM rate
+        pk, src = peak("bf16_tflops_sustained")
         fw = max(1, prof.forwards)
         total = prof.gemm_ms + prof.attn_ms + prof.norm_ms + prof.other_ms
         share = {k: getattr(prof, k) / total for k in ("gemm_ms", "attn_ms", "norm_ms", "other_ms")}
@@ -477,7 +479,7 @@ class Transformer:
                 "frac": round(ach / pk, 4), "traffic": profiled_traffic(self.kernel),
                 "traffic_note": "ncu DRAM bytes per GEMM launch, mean over the 33 GEMMs of a B=8 forward",
                 "algorithmic_flops_per_launch": round(per_launch), "gemm_flops_per_forward": round(gemm_flops),
-                "peak_source": src + " (burst)", "kernel": "gemm_bf16_tc2_kernel (all GEMMs of the forward)",
+                "peak_source": src + " (sustained)", "kernel": "gemm_bf16_tc2_kernel (all GEMMs of the forward)",
                 "share_of_forward": round(share["gemm_ms"], 4),
                 "attention_tflops": round(attn_flops / (share["attn_ms"] * ms_per_step * 1e-3) / 1e12, 1)
                 if prof.attn_ms else None,
