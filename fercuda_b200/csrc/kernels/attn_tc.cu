@@ -26,6 +26,7 @@
 // exp(s - max) / sum with P rounded to bf16 before P.V).
 // Every wait is bounded (about one second): on timeout the kernel records an
 // error bit, stops, releases tensor memory and returns. No TMA multicast.
+#include "f32x2.cuh"
 #include "pdl.cuh"
 #include "sm100_util.cuh"
 #include "tmap.cuh"
@@ -351,18 +352,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             }
             fence_after();
             // p = 2^(s*scale - m_new), row sum, P (bf16) into shared memory
-            float sm[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sm[e] = 0.0f;
+            // on packed pairs: s*scale - m_new is one fma per element and the
+            // eight row-sum accumulators are four pairs, each element added
+            // to the same accumulator in the same order as the scalar form,
+            // so the bits are those of fmaf / scalar adds
+            uint64_t sm2[4] = {0, 0, 0, 0};
+            const uint64_t sc2 = f2_splat(scale_log2), nm2 = f2_splat(-m_new);
 #pragma unroll
             for (int c = 0; c < TK / 32; ++c) {
                 uint32_t w[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    const float p0 = ex2(fmaf(sv[c * 32 + e], scale_log2, -m_new));
-                    const float p1 = ex2(fmaf(sv[c * 32 + e + 1], scale_log2, -m_new));
-                    sm[e & 7] += p0;
-                    sm[(e + 1) & 7] += p1;
+                    float t0, t1;
+                    f2_unpack(f2_fma(f2_pack(sv[c * 32 + e], sv[c * 32 + e + 1]), sc2, nm2), t0, t1);
+                    const float p0 = ex2(t0), p1 = ex2(t1);
+                    sm2[(e >> 1) & 3] = f2_add(sm2[(e >> 1) & 3], f2_pack(p0, p1));
                     w[e >> 1] = pack_bf16x2(p0, p1);
                 }
                 const uint32_t prow = sbase + OFF_P + r * 128;
@@ -373,6 +377,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                                  w[4 * q4 + 3]);
                 }
             }
+            float sm[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) f2_unpack(sm2[k], sm[2 * k], sm[2 * k + 1]);
             const float sum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
             // O holds sum_{i<j} P_i V_i scaled by 2^-m: rescale it in place
             // before P_j V_j accumulates on it.
@@ -381,8 +388,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 for (int c = 0; c < 2; ++c) {
                     float ov[32];
                     tmem_ld32(trow + COL_O + c * 32, ov);
+                    const uint64_t a2 = f2_splat(alpha);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+                    for (int e = 0; e < 32; e += 2) {
+                        float o0, o1;
+                        f2_unpack(f2_mul(f2_pack(ov[e], ov[e + 1]), a2), o0, o1);
+                        ov[e] = o0;
+                        ov[e + 1] = o1;
+                    }
                     tmem_st32(trow + COL_O + c * 32, ov);
                 }
             }
