@@ -18,9 +18,10 @@
 //               max in the log2 domain, p = 2^(s*scale - m) (ex2.approx), row
 //               sum in f32, P rounded to bf16 into swizzled shared memory (the
 //               A operand of the P.V MMA). O accumulates in tensor memory
-//               across key blocks; when a row's max grows the softmax thread
-//               rescales its O row in place (tcgen05.ld / st) before the
-//               next P.V lands on it.
+//               across key blocks; the max a row subtracts is raised only
+//               when a block's max exceeds it by more than 2^8, and then the
+//               softmax thread rescales its O row in place (tcgen05.ld / st)
+//               before the next P.V lands on it.
 // Finally o / l is rounded to bf16 and stored. The arithmetic is the same
 // online softmax as the mma.sync kernel in xfmr_kernels.cu (and the oracle's
 // exp(s - max) / sum with P rounded to bf16 before P.V).
@@ -56,6 +57,7 @@ constexpr int kThreads = 192;
 constexpr int kCtasPerSm = 3;
 constexpr uint32_t TMEM_COLS = 128;       // S at columns [0, 64), O at [64, 128)
 constexpr uint32_t COL_O = 64;
+constexpr float kRescaleSlack = 8.0f;     // log2 units the subtracted max may lag the row max
 static_assert(kCtasPerSm * TMEM_COLS <= 512, "tensor memory per SM");
 
 // kind::f16 instruction descriptors: f32 accumulate, bf16 A and B, M = 128.
@@ -342,8 +344,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             for (int e = 8; e < TK; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[e]);
             const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-            const float m_new = fmaxf(m, smax * scale_log2);
-            const float alpha = ex2(m - m_new);
+            // The subtracted max is raised only when the block's max exceeds
+            // it by more than kRescaleSlack (log2 units, so p <= 256):
+            // softmax does not depend on the constant subtracted, and O is
+            // then rescaled a few times per row instead of whenever the max
+            // grows (always on the first block with a key).
+            const float bmax = smax * scale_log2;
+            const bool raise = bmax > m + kRescaleSlack;
+            const float m_new = raise ? bmax : m;
+            const float alpha = raise ? ex2(m - m_new) : 1.0f;   // 0 while m is -inf
             // P_{j-1} V_{j-1} done: P's buffer is free and O holds every
             // earlier block
             if (j > 0 && !warp_wait(&bars.o_full, ph ^ 1u)) {
