@@ -224,6 +224,7 @@ fer_status_t fer_buffer_row_digests(fer_session_t* session, uint64_t buffer, uin
     const Buffer* b = S.find(buffer);
     if (!b) return not_found("buffer id not found");
     if (rows == 0 || row_bytes == 0 || row_bytes % 16) return invalid("row_bytes must be a nonzero multiple of 16");
+    if (rows > 65535u) return invalid("at most 65535 rows per call");
     if (row_bytes * rows > b->bytes) return invalid("rows x row_bytes exceeds the buffer");
     if (reinterpret_cast<uintptr_t>(b->ptr) % 16) return invalid("buffer is not 16-byte aligned");
     void* dev = nullptr;

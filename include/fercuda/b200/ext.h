@@ -178,7 +178,8 @@ fer_status_t fer_transformer_shard(uint32_t global_batch, int32_t world, int32_t
  * multiple of 16) of a buffer: the sum mod 2^64 of a mixing hash of every
  * 16-byte chunk and its position within the row, so it depends only on the
  * row's bytes (not on the row's index or the order of summation). Used to
- * compare logits across ranks and GPU counts bit for bit. Synchronous. */
+ * compare logits across ranks and GPU counts bit for bit. Synchronous;
+ * rows <= 65535 per call. */
 fer_status_t fer_buffer_row_digests(fer_session_t* session, uint64_t buffer, uint64_t row_bytes, uint32_t rows,
                                     uint64_t* out_digests);
 
