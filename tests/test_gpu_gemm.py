@@ -121,3 +121,41 @@ def test_gemm_argument_errors(session):
     with pytest.raises(capi.FerError) as e:
         session.gemm(bx, b2, bo)
     assert e.value.code == capi.FER_STATUS_INVALID_ARGUMENT
+
+
+def test_gemm_8192_full_matrix_vs_reference_kernel():
+    """The configured GEMM (8192^3, bf16 operands N(0, 1/sqrt(K)) from seed 3,
+    made by the device generator as the benchmark does) against the
+    reference's own GEMM kernel (k_matmul_f32 through fer::ops::matmul,
+    src/runtime/ops_bridge.cu:13-31, built from the reference sources) run on
+    the same operands upcast to f32: every one of the 67M outputs, not a
+    sample. The reference kernel's sequential fmaf chain and the tensor-core
+    accumulation differ only in summation order."""
+    import torch
+
+    ref = oracle_lib.ref_kernels()
+    assert ref is not None, "oracle/_ref/libref_kernels.so missing (build() compiles it)"
+    n = 8192
+    ab = torch.empty(2 * n * n, dtype=torch.int16, device="cuda")
+    rc = capi.kernels().fer_fill_normal_bf16(C.c_void_p(ab.data_ptr()), 2 * n * n, synth.GEMM["seed"],
+                                             C.c_float(1.0 / np.sqrt(n)), None)
+    assert rc == 0
+    a_bits, b_bits = ab[: n * n], ab[n * n:]
+    ours = torch.empty(n * n, dtype=torch.float32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    k = capi.kernels()
+    k.fer_gemm_bf16_tc_ex.argtypes = [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_void_p, C.c_void_p]
+    k.fer_gemm_bf16_tc_ex.restype = C.c_int
+    assert k.fer_gemm_bf16_tc_ex(a_bits.data_ptr(), b_bits.data_ptr(), ours.data_ptr(), None, n, n, n, 0,
+                                 err.data_ptr(), None) == 0
+    af = a_bits.view(torch.bfloat16).float()
+    bf = b_bits.view(torch.bfloat16).float()
+    theirs = torch.empty(n * n, dtype=torch.float32, device="cuda")
+    ref.refshim_matmul_f32(C.c_void_p(af.data_ptr()), C.c_void_p(bf.data_ptr()), C.c_void_p(theirs.data_ptr()),
+                           n, n, n, None)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.isfinite(ours).all()
+    e = float((ours.double() - theirs.double()).abs().max() / theirs.double().abs().max())
+    assert e <= REQUIRED_TOL
+    assert e <= REL, e
