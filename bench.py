@@ -413,7 +413,7 @@ class Transformer:
         self.bl = s.alloc(capi.FER_DTYPE_F32, [self.B_local, S, V])
         s.upload(self.bt, self.toks)
         self.units_per_step = self.global_tokens
-        self.launches_per_step = 3 + 7 * L
+        self.launches_per_step = 2 + 7 * L     # embed+LN1, 7 per layer, final LN, LM head
         self.h2d = 4 * T
         self.d2h = 4 * T * V
 

@@ -190,6 +190,8 @@ cudaError_t fer_fill_normal_bf16(void* out, size_t n, uint64_t seed, float stdde
 cudaError_t fer_fill_f32(float* out, size_t n, float v, cudaStream_t s);
 cudaError_t fer_embed_f32(const int* tok, const void* emb, float* x, int T, int d, int vocab, uint32_t* err,
                           cudaStream_t s);
+cudaError_t fer_embed_ln_bf16(const int* tok, const void* emb, float* x, const float* g, const float* b, void* out,
+                              int T, int d, int vocab, float eps, uint32_t* err, cudaStream_t s);
 cudaError_t fer_ln_bf16(const float* x, const float* g, const float* b, void* out, int T, int d, float eps,
                         cudaStream_t s);
 cudaError_t fer_rows_fast_f32(const float* x, float* y, const float* gamma, const float* beta, int rows, int cols,

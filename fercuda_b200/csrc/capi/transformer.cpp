@@ -276,13 +276,18 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
     // causal attention: S(S+1)/2 (query, key) pairs per sequence and head, 2*64 flops each for QK^T and for PV
     const double ga = 4.0 * 64.0 * (static_cast<double>(Sq) * (Sq + 1) / 2.0) * B * c.heads;
     auto issue = [&]() {
-        run(3, 0.0, [&] { return fer_embed_f32(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, Ti, d, V, err, st); });
         for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
             const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
             const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
             const float* g2 = m->ln + (4 * l + 2) * static_cast<size_t>(d);
             const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
-            run(2, 0.0, [&] { return fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st); });
+            if (l == 0)   // embedding and the first layer norm in one pass
+                run(2, 0.0, [&] {
+                    return fer_embed_ln_bf16(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, g1, b1, m->a, Ti,
+                                             d, V, c.eps, err, st);
+                });
+            else
+                run(2, 0.0, [&] { return fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st); });
             run(0, gq, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_qkv[l], m->qkv, nullptr, Ti, 3 * d, d, kEpiBF16, err, st); });
             run(1, ga, [&] { return fer_attn_causal_ex(m->qkv, m->att, B, Sq, d, static_cast<int>(c.heads), 0, err, st); });
             run(0, go, [&] { return fer_gemm_bf16_tc_ex(m->att, W + m->off_o[l], m->x, m->x, Ti, d, d, kEpiResidF32, err, st); });
@@ -475,7 +480,7 @@ fer_status_t fer_transformer_prefill(fer_session_t* session, uint64_t model, uin
     cudaStream_t st = S.stream;
     uint32_t* err = S.dev_err;
     const uint16_t* W = m->W;
-    cudaError_t e = fer_embed_f32(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, Ti, d, V, err, st);
+    cudaError_t e = cudaSuccess;
     for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
         const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
         const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
@@ -483,7 +488,9 @@ fer_status_t fer_transformer_prefill(fer_session_t* session, uint64_t model, uin
         const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
         uint16_t* kcache = kc.kv + 2 * l * kc.layer_elems;
         uint16_t* vcache = kcache + kc.layer_elems;
-        e = fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st);
+        e = l == 0 ? fer_embed_ln_bf16(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, g1, b1, m->a, Ti, d, V,
+                                       c.eps, err, st)
+                   : fer_ln_bf16(m->x, g1, b1, m->a, Ti, d, c.eps, st);
         if (e == cudaSuccess)
             e = fer_gemm_bf16_tc_ex(m->a, W + m->off_qkv[l], m->qkv, nullptr, Ti, 3 * d, d, kEpiBF16, err, st);
         if (e == cudaSuccess)
@@ -560,7 +567,6 @@ fer_status_t fer_transformer_decode(fer_session_t* session, uint64_t model, uint
     };
     cudaError_t e = cudaSuccess;
     auto issue = [&]() {
-        e = fer_embed_f32(kc.tok_stage, W + m->off_emb, m->x, B, d, V, err, st);
         for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
             const float* g1 = m->ln + (4 * l + 0) * static_cast<size_t>(d);
             const float* b1 = m->ln + (4 * l + 1) * static_cast<size_t>(d);
@@ -568,7 +574,8 @@ fer_status_t fer_transformer_decode(fer_session_t* session, uint64_t model, uint
             const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
             uint16_t* kcache = kc.kv + 2 * l * kc.layer_elems;
             uint16_t* vcache = kcache + kc.layer_elems;
-            e = fer_ln_bf16(m->x, g1, b1, m->a, B, d, c.eps, st);
+            e = l == 0 ? fer_embed_ln_bf16(kc.tok_stage, W + m->off_emb, m->x, g1, b1, m->a, B, d, V, c.eps, err, st)
+                       : fer_ln_bf16(m->x, g1, b1, m->a, B, d, c.eps, st);
             if (e == cudaSuccess) e = gemm(m->a, W + m->off_qkv[l], m->qkv, 3 * d, d, kEpiBF16);
             if (e == cudaSuccess)
                 e = fer_decode_kv_attention(m->qkv, kcache, vcache, m->att, kc.scratch, kc.attn_counters, B, d, H,

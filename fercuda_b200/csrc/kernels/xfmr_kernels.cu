@@ -9,6 +9,8 @@
 //                      generator), so a 333 MB model is made in milliseconds
 //                      and only rank 0's copy is broadcast
 //   embed_f32          token rows of the bf16 embedding -> f32 residual stream
+//   embed_ln_bf16      the same rows and, in the same pass, the first layer's
+//                      layer norm of them (one launch instead of two)
 //   ln_bf16            per-token layer norm, f32 in, bf16 out (GEMM operand)
 //   attn_causal        causal multi-head attention for head_dim 64 straight out
 //                      of the fused QKV activation [tokens, 3*d]; flash-style
@@ -153,6 +155,61 @@ __global__ void ln_bf16(const float* __restrict__ x, const float* __restrict__ g
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
         v[i] = *reinterpret_cast<const float4*>(row + (i * 32 + lane) * 4);
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / static_cast<float>(d);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+        q += (a * a + bb * bb) + (c * c + e * e);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float inv = rsqrtf(q / static_cast<float>(d) + eps);
+    bf16* orow = out + static_cast<size_t>(warp) * d;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        const float4 gg = *reinterpret_cast<const float4*>(g + c);
+        const float4 bb = *reinterpret_cast<const float4*>(b + c);
+        __nv_bfloat162 p0 = __floats2bfloat162_rn((v[i].x - mean) * inv * gg.x + bb.x, (v[i].y - mean) * inv * gg.y + bb.y);
+        __nv_bfloat162 p1 = __floats2bfloat162_rn((v[i].z - mean) * inv * gg.z + bb.z, (v[i].w - mean) * inv * gg.w + bb.w);
+        uint2 w;
+        w.x = *reinterpret_cast<uint32_t*>(&p0);
+        w.y = *reinterpret_cast<uint32_t*>(&p1);
+        *reinterpret_cast<uint2*>(orow + c) = w;
+    }
+}
+
+// Token embedding and the first layer's layer norm in one pass: one warp per
+// token writes the f32 residual row (the bf16 embedding row upcast, exactly
+// what embed_f32 writes) and its layer norm (the arithmetic of ln_bf16, on
+// the same values in the same lanes, so the same bits).
+template <int VPL>
+__global__ void embed_ln_bf16(const int* __restrict__ tok, const bf16* __restrict__ emb, float* __restrict__ x,
+                              const float* __restrict__ g, const float* __restrict__ b, bf16* __restrict__ out, int T,
+                              int d, int vocab, float eps, uint32_t* err) {
+    fer::dev::pdl_begin();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const int id = tok[warp];
+    const bool bad = id < 0 || id >= vocab;
+    if (bad && lane == 0) fer::dev::report(err, fer::dev::kErrBadShape);
+    const bf16* src = emb + static_cast<size_t>(bad ? 0 : id) * d;
+    float* row = x + static_cast<size_t>(warp) * d;
+    float4 v[VPL];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        const uint2 u = *reinterpret_cast<const uint2*>(src + c);
+        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const float2 f0 = __bfloat1622float2(p[0]), f1 = __bfloat1622float2(p[1]);
+        v[i] = bad ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(f0.x, f0.y, f1.x, f1.y);
+        *reinterpret_cast<float4*>(row + c) = v[i];
         s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
     }
 #pragma unroll
@@ -416,6 +473,25 @@ extern "C" cudaError_t fer_ln_bf16(const float* x, const float* g, const float* 
         case 8: if (d == 1024) { e = fer::host::launch_pdl(ln_bf16<8>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
         case 16: if (d == 2048) { e = fer::host::launch_pdl(ln_bf16<16>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
         case 32: if (d == 4096) { e = fer::host::launch_pdl(ln_bf16<32>, grid, block, 0, s, x, g, b, o, T, d, eps); break; } return cudaErrorInvalidValue;
+        default: return cudaErrorInvalidValue;
+    }
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+extern "C" cudaError_t fer_embed_ln_bf16(const int* tok, const void* emb, float* x, const float* g, const float* b,
+                                         void* out, int T, int d, int vocab, float eps, uint32_t* err,
+                                         cudaStream_t s) {
+    const int wpb = 8;
+    const dim3 grid((T + wpb - 1) / wpb), block(32 * wpb);
+    const bf16* em = static_cast<const bf16*>(emb);
+    bf16* o = static_cast<bf16*>(out);
+    cudaError_t e = cudaSuccess;
+    switch (d) {
+        case 256: e = fer::host::launch_pdl(embed_ln_bf16<2>, grid, block, 0, s, tok, em, x, g, b, o, T, d, vocab, eps, err); break;
+        case 512: e = fer::host::launch_pdl(embed_ln_bf16<4>, grid, block, 0, s, tok, em, x, g, b, o, T, d, vocab, eps, err); break;
+        case 1024: e = fer::host::launch_pdl(embed_ln_bf16<8>, grid, block, 0, s, tok, em, x, g, b, o, T, d, vocab, eps, err); break;
+        case 2048: e = fer::host::launch_pdl(embed_ln_bf16<16>, grid, block, 0, s, tok, em, x, g, b, o, T, d, vocab, eps, err); break;
+        case 4096: e = fer::host::launch_pdl(embed_ln_bf16<32>, grid, block, 0, s, tok, em, x, g, b, o, T, d, vocab, eps, err); break;
         default: return cudaErrorInvalidValue;
     }
     return e != cudaSuccess ? e : cudaGetLastError();
