@@ -152,3 +152,60 @@ def test_two_gpu_broadcast_and_sharded_forward():
     gathered = [d for r in res for d in r[3]]
     assert gathered == res[0][4], "sharded logits differ from the one-GPU forward"
     assert all(r[5] == 0 for r in res)
+
+
+def test_comm_argument_errors(session):
+    uid = capi.comm_unique_id()
+    for rank, world in ((1, 1), (-1, 2), (0, 0)):
+        with pytest.raises(capi.FerError) as e:
+            session.comm_init(uid, rank, world)
+        assert e.value.code == capi.FER_STATUS_INVALID_ARGUMENT
+    with pytest.raises(capi.FerError) as e:
+        session.row_digests(1 << 40, 16, 1)              # no such buffer
+    assert e.value.code == capi.FER_STATUS_NOT_FOUND
+
+
+def _lonely_rank(q_out):
+    import time
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    with capi.Session(0, pool_bytes=256 << 20) as s:
+        t0 = time.time()
+        try:
+            s.comm_init(capi.comm_unique_id(), 0, 2, 3_000)
+            first = (None, "", 0.0)
+        except capi.FerError as e:
+            first = (e.code, e.msg, time.time() - t0)
+        m = capi.Transformer(s, 1, 256, 4, 512, 1000, 64)
+        m.init_weights(4, 0.02)
+        s.comm_init(capi.comm_unique_id(), 0, 1, 30_000)
+        sent = m.broadcast_weights(0)
+        s.comm_destroy()
+        q_out.put(first + (sent == 2 * m.weight_elements(), s.device_errors()))
+        m.close()
+
+
+def test_rank_that_never_joins_times_out():
+    """Failure made on the host: a two-rank communicator whose second rank
+    never calls fer_comm_init. The first rank's init returns
+    FER_STATUS_INTERNAL_ERROR after its 3 s timeout (the communicator is
+    aborted) instead of waiting forever, and the session stays usable: a
+    one-rank communicator and a weight broadcast work right after. No kernel
+    waits on the missing rank at any point; the rank runs in a child process
+    so that the test itself is bounded too."""
+    import torch
+
+    ctx = torch.multiprocessing.get_context("spawn")
+    q_out = ctx.Queue()
+    p = ctx.Process(target=_lonely_rank, args=(q_out,))
+    p.start()
+    try:
+        code, msg, waited, sent_ok, errors = q_out.get(timeout=240)
+    finally:
+        p.join(timeout=60)
+        if p.exitcode is None:
+            p.kill()
+    assert p.exitcode == 0
+    assert code == capi.FER_STATUS_INTERNAL_ERROR and "timed out" in msg, (code, msg)
+    assert 2.5 <= waited <= 60.0, waited
+    assert sent_ok and errors == 0
