@@ -11,6 +11,8 @@ import ctypes as C
 import os
 from pathlib import Path
 
+import numpy as np
+
 PKG = Path(__file__).resolve().parent
 LIBDIR = PKG / "lib"
 
@@ -277,6 +279,7 @@ CAPI_PROTOTYPES = {
     "fer_transformer_init_weights": (S, [P, u64, u64, f32]),
     "fer_transformer_weight_buffer": (S, [P, u64, pu64]),
     "fer_transformer_forward": (S, [P, u64, u64, u64, pu64]),
+    "fer_transformer_forward_host": (S, [P, u64, P, u32, u32, P, u32]),
     "fer_transformer_destroy": (S, [P, u64]),
     "fer_transformer_profile": (S, [P, u64, u32]),
     "fer_transformer_profile_read": (S, [P, u64, C.POINTER(fer_transformer_profile_t)]),
@@ -602,6 +605,22 @@ class Transformer:
         job = C.c_uint64()
         check("fer_transformer_forward", self.s.call("fer_transformer_forward", self.id, tokens, logits, C.byref(job)))
         return job.value
+
+    def forward_host(self, tokens: np.ndarray, logits: np.ndarray, chunk_seqs: int = 0) -> None:
+        """fer_transformer_forward_host: host i32 tokens [batch, seq] in, host
+        f32 logits [batch, seq, vocab] (any C-contiguous shape of that size)
+        out, the D2H copy of each chunk of sequences overlapped with the
+        next chunk's forward. Returns when the logits are in `logits`."""
+        if tokens.dtype != np.int32 or tokens.ndim != 2 or not tokens.flags.c_contiguous:
+            raise ValueError("tokens must be a C-contiguous int32 [batch, seq] array")
+        if logits.dtype != np.float32 or not logits.flags.c_contiguous or not logits.flags.writeable:
+            raise ValueError("logits must be a writeable C-contiguous float32 array")
+        b, n = tokens.shape
+        if logits.size != b * n * self.cfg.vocab:
+            raise ValueError(f"logits must hold batch x seq x vocab = {b * n * self.cfg.vocab} floats")
+        check("fer_transformer_forward_host",
+              self.s.call("fer_transformer_forward_host", self.id, tokens.ctypes.data, b, n, logits.ctypes.data,
+                          chunk_seqs))
 
     def kv_create(self, max_batch: int, max_seq: int) -> int:
         cid = C.c_uint64()

@@ -18,6 +18,7 @@
 
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <unordered_map>
@@ -77,6 +78,13 @@ struct Transformer {
     std::vector<Graph> graphs;
     bool graphs_off = false;
     std::unordered_map<uint64_t, KvCache> caches;
+    // fer_transformer_forward_host: two staging slots for chunk tokens and
+    // logits, the stream their D2H copies run on, and per-slot events
+    int* stage_tok[2] = {nullptr, nullptr};
+    float* stage_logits[2] = {nullptr, nullptr};
+    size_t stage_tokens = 0;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t computed[2] = {nullptr, nullptr}, copied[2] = {nullptr, nullptr};
 
     void free_cache(KvCache& kc) {
         if (kc.graph) cudaGraphExecDestroy(kc.graph);
@@ -113,6 +121,16 @@ struct Transformer {
             if (g.exec) cudaGraphExecDestroy(g.exec);
         release_marks();
         for (cudaEvent_t e : spare) cudaEventDestroy(e);
+        if (copy_stream) {
+            cudaStreamSynchronize(copy_stream);
+            cudaStreamDestroy(copy_stream);
+        }
+        for (int s = 0; s < 2; ++s) {
+            for (cudaEvent_t e : {computed[s], copied[s]})
+                if (e) cudaEventDestroy(e);
+            for (void* p : {static_cast<void*>(stage_tok[s]), static_cast<void*>(stage_logits[s])})
+                if (p) gpu_hot_free(S->pool, p);
+        }
         for (void* p : {static_cast<void*>(x), static_cast<void*>(a), static_cast<void*>(qkv),
                         static_cast<void*>(att), static_cast<void*>(hid), static_cast<void*>(ln)})
             if (p) gpu_hot_free(S->pool, p);
@@ -234,23 +252,17 @@ fer_status_t fer_transformer_weight_buffer(fer_session_t* session, uint64_t mode
     return ok();
 }
 
-fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uint64_t tokens, uint64_t logits,
-                                     uint64_t* out_job_id) {
-    if (!session) return invalid("session is null");
-    Session& S = session->impl;
-    Transformer* m = find_model(S, model);
-    if (!m) return not_found("model id not found");
-    const Buffer* tb = S.find(tokens);
-    const Buffer* lb = S.find(logits);
-    if (!tb || !lb) return not_found("buffer id not found");
-    if (tb->desc.dtype != FER_DTYPE_I32 || (tb->desc.rank != 1 && tb->desc.rank != 2))
-        return invalid("tokens must be i32 [batch, seq] or [seq]");
-    const int B = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[0]) : 1;
-    const int Sq = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[1]) : static_cast<int>(tb->desc.dims[0]);
+}  // extern "C"
+
+namespace {
+
+// Queues one forward of B sequences of Sq tokens (tok: device i32 [B*Sq];
+// logits: device f32 [B*Sq, vocab]) on the session stream: eager on the
+// first use of a (tok, logits, B, Sq) signature, captured into a CUDA graph
+// on the second, replayed after that.
+cudaError_t forward_ptrs(Session& S, Transformer* m, const int* tok, float* logits, int B, int Sq) {
     const size_t T = static_cast<size_t>(B) * Sq;
     const fer_transformer_config_t& c = m->cfg;
-    if (T > c.max_tokens) return invalid("batch * seq exceeds the model's max_tokens");
-    if (lb->desc.dtype != FER_DTYPE_F32 || lb->numel != T * c.vocab) return invalid("logits must be f32 [batch, seq, vocab]");
     const int d = static_cast<int>(c.d_model), F = static_cast<int>(c.ffn), V = static_cast<int>(c.vocab);
     const int Ti = static_cast<int>(T);
     cudaStream_t st = S.stream;
@@ -283,7 +295,7 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
             const float* b2 = m->ln + (4 * l + 3) * static_cast<size_t>(d);
             if (l == 0)   // embedding and the first layer norm in one pass
                 run(2, 0.0, [&] {
-                    return fer_embed_ln_bf16(static_cast<const int*>(tb->ptr), W + m->off_emb, m->x, g1, b1, m->a, Ti,
+                    return fer_embed_ln_bf16(tok, W + m->off_emb, m->x, g1, b1, m->a, Ti,
                                              d, V, c.eps, err, st);
                 });
             else
@@ -298,7 +310,7 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
         const float* gf = m->ln + (4 * static_cast<size_t>(c.layers)) * d;
         const float* bf = gf + d;
         run(2, 0.0, [&] { return fer_ln_bf16(m->x, gf, bf, m->a, Ti, d, c.eps, st); });
-        run(0, glm, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_lm, lb->ptr, nullptr, Ti, V, d, kEpiF32, err, st); });
+        run(0, glm, [&] { return fer_gemm_bf16_tc_ex(m->a, W + m->off_lm, logits, nullptr, Ti, V, d, kEpiF32, err, st); });
     };
     static const int graphs_env = [] {
         const char* ev = std::getenv("FERCUDA_XFMR_GRAPH");
@@ -307,9 +319,9 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
     Transformer::Graph* g = nullptr;
     if (!m->profiling && graphs_env && !m->graphs_off) {
         for (auto& x : m->graphs)
-            if (x.tokens == tb->ptr && x.logits == lb->ptr && x.B == B && x.Sq == Sq) g = &x;
+            if (x.tokens == tok && x.logits == logits && x.B == B && x.Sq == Sq) g = &x;
         if (!g && m->graphs.size() < 8) {
-            m->graphs.push_back(Transformer::Graph{tb->ptr, lb->ptr, B, Sq, nullptr});   // first use: eager
+            m->graphs.push_back(Transformer::Graph{tok, logits, B, Sq, nullptr});   // first use: eager
         } else if (g && !g->exec) {
             // second use: capture the 59 launches once
             cudaGraph_t graph = nullptr;
@@ -334,12 +346,135 @@ fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uin
     }
     if (g && g->exec) e = cudaGraphLaunch(g->exec, st);
     else issue();
-    if (e != cudaSuccess) {
+    if (e == cudaSuccess && m->profiling) m->prof.forwards++;
+    return e;
+}
+
+// Chunk size of fer_transformer_forward_host when the caller passes 0: at
+// most about 4096 tokens (8 sequences of 512) and at least four chunks when
+// the batch allows (only the first chunk's forward is not under a copy),
+// within max_tokens.
+uint32_t default_chunk(const fer_transformer_config_t& c, uint32_t batch, uint32_t seq) {
+    uint32_t k = seq >= 4096 ? 1u : 4096u / seq;
+    k = std::min<uint32_t>(k, (batch + 3) / 4);
+    k = std::min<uint32_t>(k, std::max<uint32_t>(1u, c.max_tokens / seq));
+    return std::max<uint32_t>(1u, std::min(k, batch));
+}
+
+}  // namespace
+
+extern "C" {
+
+fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uint64_t tokens, uint64_t logits,
+                                     uint64_t* out_job_id) {
+    if (!session) return invalid("session is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    const Buffer* tb = S.find(tokens);
+    const Buffer* lb = S.find(logits);
+    if (!tb || !lb) return not_found("buffer id not found");
+    if (tb->desc.dtype != FER_DTYPE_I32 || (tb->desc.rank != 1 && tb->desc.rank != 2))
+        return invalid("tokens must be i32 [batch, seq] or [seq]");
+    const int B = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[0]) : 1;
+    const int Sq = tb->desc.rank == 2 ? static_cast<int>(tb->desc.dims[1]) : static_cast<int>(tb->desc.dims[0]);
+    const size_t T = static_cast<size_t>(B) * Sq;
+    const fer_transformer_config_t& c = m->cfg;
+    if (T > c.max_tokens) return invalid("batch * seq exceeds the model's max_tokens");
+    if (lb->desc.dtype != FER_DTYPE_F32 || lb->numel != T * c.vocab) return invalid("logits must be f32 [batch, seq, vocab]");
+    if (forward_ptrs(S, m, static_cast<const int*>(tb->ptr), static_cast<float*>(lb->ptr), B, Sq) != cudaSuccess) {
         cudaGetLastError();
         return internal("kernel launch failed");
     }
-    if (m->profiling) m->prof.forwards++;
     return S.make_job({}, out_job_id);
+}
+
+fer_status_t fer_transformer_forward_host(fer_session_t* session, uint64_t model, const int32_t* host_tokens,
+                                          uint32_t batch, uint32_t seq, float* host_logits, uint32_t chunk_seqs) {
+    if (!session) return invalid("session is null");
+    if (!host_tokens || !host_logits) return invalid("host_tokens or host_logits is null");
+    Session& S = session->impl;
+    Transformer* m = find_model(S, model);
+    if (!m) return not_found("model id not found");
+    const fer_transformer_config_t& c = m->cfg;
+    if (batch == 0 || seq == 0) return invalid("batch and seq must be > 0");
+    if (seq > c.max_tokens) return invalid("seq exceeds the model's max_tokens");
+    const uint32_t k = chunk_seqs ? chunk_seqs : default_chunk(c, batch, seq);
+    if (static_cast<size_t>(k) * seq > c.max_tokens) return invalid("chunk_seqs * seq exceeds the model's max_tokens");
+    const uint32_t kk = std::min(k, batch);
+    const size_t chunk_T = static_cast<size_t>(kk) * seq;
+    const size_t V = c.vocab;
+    // two staging slots (tokens + logits); chunk i uses slot i % 2
+    if (m->stage_tokens < chunk_T) {
+        for (int s = 0; s < 2; ++s) {
+            if (m->stage_tok[s]) gpu_hot_free(S.pool, m->stage_tok[s]);
+            if (m->stage_logits[s]) gpu_hot_free(S.pool, m->stage_logits[s]);
+            m->stage_tok[s] = static_cast<int*>(pool_alloc(S, chunk_T * 4));
+            m->stage_logits[s] = static_cast<float*>(pool_alloc(S, chunk_T * V * 4));
+        }
+        m->stage_tokens = chunk_T;
+        if (!m->stage_tok[0] || !m->stage_tok[1] || !m->stage_logits[0] || !m->stage_logits[1]) {
+            for (int s = 0; s < 2; ++s) {
+                if (m->stage_tok[s]) gpu_hot_free(S.pool, m->stage_tok[s]);
+                if (m->stage_logits[s]) gpu_hot_free(S.pool, m->stage_logits[s]);
+                m->stage_tok[s] = nullptr;
+                m->stage_logits[s] = nullptr;
+            }
+            m->stage_tokens = 0;
+            return internal("staging allocation failed (session pool too small)");
+        }
+    }
+    if (!m->copy_stream && cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        m->copy_stream = nullptr;
+        cudaGetLastError();
+        return internal("cudaStreamCreate failed");
+    }
+    for (int s = 0; s < 2; ++s)
+        for (cudaEvent_t* ev : {&m->computed[s], &m->copied[s]})
+            if (!*ev && cudaEventCreateWithFlags(ev, cudaEventDisableTiming) != cudaSuccess) {
+                *ev = nullptr;
+                cudaGetLastError();
+                return internal("cudaEventCreate failed");
+            }
+    const cudaStream_t cs = S.stream, ds = m->copy_stream;
+    const uint32_t chunks = (batch + kk - 1) / kk;
+    cudaError_t e = cudaSuccess;
+    // D2H of chunk i, on the copy stream after its forward; the forward of
+    // chunk i+1 is queued first, so it runs under this copy even when the
+    // host buffer is pageable (a pageable copy returns only when done)
+    auto drain = [&](uint32_t i) {
+        const int s = static_cast<int>(i & 1);
+        const size_t seqs = std::min<size_t>(kk, batch - static_cast<size_t>(i) * kk);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(ds, m->computed[s], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(host_logits + static_cast<size_t>(i) * chunk_T * V, m->stage_logits[s],
+                                seqs * seq * V * 4, cudaMemcpyDeviceToHost, ds);
+        if (e == cudaSuccess) e = cudaEventRecord(m->copied[s], ds);
+    };
+    for (uint32_t i = 0; i < chunks && e == cudaSuccess; ++i) {
+        const int s = static_cast<int>(i & 1);
+        const size_t seqs = std::min<size_t>(kk, batch - static_cast<size_t>(i) * kk);
+        // slot s is free once chunk i-2's logits have left the device
+        if (i >= 2) e = cudaStreamWaitEvent(cs, m->copied[s], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(m->stage_tok[s], host_tokens + static_cast<size_t>(i) * chunk_T, seqs * seq * 4,
+                                cudaMemcpyHostToDevice, cs);
+        if (e == cudaSuccess) e = forward_ptrs(S, m, m->stage_tok[s], m->stage_logits[s], static_cast<int>(seqs),
+                                               static_cast<int>(seq));
+        if (e == cudaSuccess) e = cudaEventRecord(m->computed[s], cs);
+        if (i >= 1) drain(i - 1);
+    }
+    if (chunks) drain(chunks - 1);
+    // the compute stream has nothing queued after the last forward's event,
+    // which the last copy waited on: the copy stream finishing means all done
+    const cudaError_t w = cudaStreamSynchronize(ds);
+    if (e == cudaSuccess) e = w;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return internal("pipelined forward failed");
+    }
+    return ok();
 }
 
 fer_status_t fer_transformer_profile(fer_session_t* session, uint64_t model, uint32_t enable) {

@@ -137,6 +137,17 @@ fer_status_t fer_transformer_weight_buffer(fer_session_t* session, uint64_t mode
  * [batch*seq, vocab]). Sequences are independent (causal within each). */
 fer_status_t fer_transformer_forward(fer_session_t* session, uint64_t model, uint64_t tokens, uint64_t logits,
                                      uint64_t* out_job_id);
+/* The forward from host memory to host memory, pipelined: host_tokens i32
+ * [batch, seq] in, host_logits f32 [batch, seq, vocab] out. The batch runs in
+ * chunks of chunk_seqs sequences (0: at most about 4096 tokens and at least
+ * four chunks where the batch allows; chunk_seqs x seq <= max_tokens); the logits of chunk i are copied to the host on a
+ * second stream while chunk i+1 computes, through two staging slots the model
+ * keeps (2 x chunk tokens x vocab x 4 bytes of the session pool). Returns
+ * when every logit is in host_logits; bit-identical to fer_transformer_forward
+ * of the whole batch followed by a download. Pinned host memory gives the
+ * full PCIe rate; pageable memory works too. */
+fer_status_t fer_transformer_forward_host(fer_session_t* session, uint64_t model, const int32_t* host_tokens,
+                                          uint32_t batch, uint32_t seq, float* host_logits, uint32_t chunk_seqs);
 fer_status_t fer_transformer_destroy(fer_session_t* session, uint64_t model);
 
 /* ---- batch-sharded forward over the GPUs of one node ------------------------

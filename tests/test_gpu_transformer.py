@@ -165,6 +165,42 @@ def test_graph_replay_is_bit_identical_to_eager(session):
     m.close()
 
 
+def test_forward_host_matches_forward_and_download(session):
+    """fer_transformer_forward_host (host tokens in, host logits out, the D2H
+    copy of chunk i overlapped with chunk i+1's forward) gives the bits of
+    fer_transformer_forward on the whole batch followed by a download: for
+    the default chunking, one sequence per chunk, ragged chunks (2, 2, 1),
+    repeated calls (eager, captured, replayed signatures), pageable and pinned
+    host memory. Bad arguments are refused."""
+    import torch
+
+    L, d, h, F, V, B, S = 2, 256, 4, 512, 1000, 5, 128
+    m = capi.Transformer(session, L, d, h, F, V, B * S)
+    m.init_weights(9, 0.02)
+    toks = tokens_for(B, S, V, 21)
+    want = run(session, m, toks, V).cpu().numpy().view(np.uint32)
+    pinned = torch.empty(B * S * V, dtype=torch.float32).pin_memory().numpy()
+    for chunk in (0, 1, 2, 3, 5, 2, 2):
+        for out in (np.full((B, S, V), np.nan, np.float32), pinned):
+            out.fill(np.nan)
+            m.forward_host(toks, out, chunk)
+            assert np.array_equal(out.reshape(B, S, V).view(np.uint32), want), chunk
+    # other tokens through the same (replayed) signatures follow the new tokens
+    toks2 = tokens_for(B, S, V, 22)
+    m.forward_host(toks2, pinned, 2)
+    want2 = run(session, m, toks2, V).cpu().numpy().view(np.uint32)
+    assert np.array_equal(pinned.reshape(B, S, V).view(np.uint32), want2)
+    with pytest.raises(capi.FerError) as e:
+        m.forward_host(toks, pinned, 6)                  # 6 x 128 > max_tokens 640
+    assert e.value.code == capi.FER_STATUS_INVALID_ARGUMENT
+    with pytest.raises(ValueError):
+        m.forward_host(toks, np.empty(7, np.float32))
+    with pytest.raises(ValueError):
+        m.forward_host(toks.astype(np.int64), pinned)
+    assert session.device_errors() == 0
+    m.close()
+
+
 def test_forward_bit_identical_over_ten_runs(session):
     """Ten forwards of the same tokens (the first eager, the second captured,
     the rest replayed, with 8-layer benchmark widths at a short sequence) give
