@@ -212,6 +212,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int seq_row0 = bseq * S;
     const int n_k = (qt + 1) * (TQ / TK);                                               // keys 0 .. end of tile
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 32) {
+        prefetch_tmap(&tmq);
+        prefetch_tmap(&tmkv);
+    }
 
     if (threadIdx.x == 0) {
         mbar_init(&bars.q_full, 1);

@@ -90,16 +90,20 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 }
 
 // Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B,
-// A K-major, B N-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
-                            (static_cast<uint32_t>(BM >> 4) << 24);
+// A K-major, B N-major, M = 128, N = n (a multiple of 16, <= 256).
+constexpr uint32_t idesc_n(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(BM >> 4) << 24);
+}
+constexpr uint32_t kIdesc = idesc_n(BN);
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate,
+                                         uint32_t idesc = kIdesc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -296,8 +300,8 @@ __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_
 
 // f32 partial tile of the cluster split-K mode: row stride in floats (the
 // 4-float pad puts 8 consecutive rows' 16-byte pieces in distinct banks).
-constexpr int kPartStride = BN + 4;
-static_assert(BM * kPartStride * 4 <= STAGES * STAGE_BYTES, "partial tile must fit the stage ring");
+constexpr int part_stride(int bn) { return bn + 4; }
+static_assert(BM * part_stride(BN) * 4 <= STAGES * STAGE_BYTES, "partial tile must fit the stage ring");
 
 // kCluster: split-K through distributed shared memory. The grid is launched
 // in clusters of `splits` CTAs; the CTAs of one cluster share one output tile
@@ -307,7 +311,13 @@ static_assert(BM * kPartStride * 4 <= STAGES * STAGE_BYTES, "partial tile must f
 // order, for its 1/splits share of the tile and stores them through the
 // epilogue directly to `out` (row-major M x N). No workspace, no second
 // kernel; the same bits as the workspace form with the same split count.
-template <bool kCluster>
+// kBN: output tile width. 256 everywhere but in the narrow cluster form
+// (128, or 64, for one M-block of at most 128 rows, the decode GEMMs): the
+// cluster reduction moves rows x kBN x 4 bytes of partials between the SMs
+// of a cluster per CTA, and that traffic, not the loads or the MMAs, is the
+// longest phase of a decode GEMM with 256-wide tiles. Each stage keeps its
+// 48 KiB slot; a narrow tile fills A plus kBN / 64 of the four B panels.
+template <bool kCluster, int kBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int epi, int splits, int kps,
@@ -316,10 +326,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ Bars bars;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
+    static_assert(kBN == 64 || kBN == 128 || kBN == BN, "tile width 64, 128 or 256");
+    static_assert(kBN == BN || kCluster, "narrow tiles only in the cluster form");
+    constexpr int kStageTx = A_BYTES + BK * kBN * 2;     // bytes the TMA loads of one stage deliver
+    constexpr int kPS = part_stride(kBN);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+    const int num_m = (M + BM - 1) / BM, num_n = (N + kBN - 1) / kBN;
     const int num_tiles = num_m * num_n;
     const int num_k = (K + BK - 1) / BK;
+    if (threadIdx.x == 32) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        if (!kCluster) prefetch_tmap(&tmC);
+    }
     // Split-K (splits > 1): job t covers k-blocks [kps * split, ...) of tile
     // t % num_tiles and stores its f32 partial at rows split * num_m * BM +
     // ... of C; splits == 1 is the plain GEMM (one job per tile, all of K).
@@ -369,8 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto load_b = [&](int s, int nb, int kblock) {
             uint8_t* sb = smem + s * STAGE_BYTES + A_BYTES;
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c)
-                tma_load_2d(sb + c * (BK * 128), &tmB, nb * BN + c * 64, kblock * BK, &bars.full[s]);
+            for (int c = 0; c < kBN / 64; ++c)
+                tma_load_2d(sb + c * (BK * 128), &tmB, nb * kBN + c * 64, kblock * BK, &bars.full[s]);
         };
         // b_static: B (weights) is not written by the previous kernel, so
         // the first job's first STAGES B tiles are fetched before the wait.
@@ -382,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             pre = nk < STAGES ? nk : STAGES;
             if (lane == 0)
                 for (int kt = 0; kt < pre; ++kt) {
-                    mbar_arrive_expect_tx(&bars.full[kt], STAGE_BYTES);
+                    mbar_arrive_expect_tx(&bars.full[kt], kStageTx);
                     load_b(kt, nb, kb0 + kt);
                 }
             __syncwarp();
@@ -408,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&bars.full[s], STAGE_BYTES);
+                    mbar_arrive_expect_tx(&bars.full[s], kStageTx);
                     tma_load_2d(smem + s * STAGE_BYTES, &tmA, (kb0 + kt) * BK, mb * BM, &bars.full[s]);
                     load_b(s, nb, kb0 + kt);
                 }
@@ -429,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+            const uint32_t d = tmem + static_cast<uint32_t>(buf * kBN);
             bool ok = true;
             for (int kt = 0; kt < nk; ++kt, ++it) {
                 const int s = it % STAGES;
@@ -450,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
                         // B: N-major, 16 K-rows of 128 bytes per step; 64-column panels 8 KiB apart.
                         const uint64_t bd = smem_desc(sb + k * 16 * 128, BK * 128, 1024);
-                        mma_bf16(d, ad, bd, (kt | k) ? 1u : 0u);
+                        mma_bf16(d, ad, bd, (kt | k) ? 1u : 0u, idesc_n(kBN));
                     }
                     mma_commit(&bars.empty[s]);   // ring slot free once these MMAs finish
                 }
@@ -467,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t stage = smem_addr(smem + STAGES * STAGE_BYTES + (warp - 2) * STAGING_BYTES);
         const bool f32_out = epi == kEpiF32 || epi == kEpiResidF32;
         const int chunk_cols = f32_out ? 32 : 64;            // one 128-byte box row
-        const int n_chunks = (BN / 2) / chunk_cols;
+        const int n_chunks = (kBN / 2) / chunk_cols;
         int local = 0;
         for (int t = blockIdx.x; t < num_jobs; t += gridDim.x, ++local) {
             const int buf = local & 1;
@@ -484,19 +503,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row_in = mb * BM + q * 32;                          // row within this job's M rows
             const int row0 = job_split(t) * num_m * BM + row_in;          // row of C (split block offset)
             const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                                   static_cast<uint32_t>(buf * BN + half * (BN / 2));
+                                   static_cast<uint32_t>(buf * kBN + half * (kBN / 2));
             if constexpr (kCluster) {
                 // f32 partial rows -> this CTA's shared memory (the stage
                 // ring is idle: every load of the one job has been consumed
                 // by MMAs that completed before acc_full)
                 const int r = q * 32 + lane;
                 const bool live = row_in + lane < M;
-                const uint32_t prow = smem_addr(smem) + static_cast<uint32_t>((r * kPartStride + half * (BN / 2)) * 4);
+                const uint32_t prow = smem_addr(smem) + static_cast<uint32_t>((r * kPS + half * (kBN / 2)) * 4);
 #pragma unroll 1
-                for (int c = 0; c < (BN / 2) / 32; ++c) {
+                for (int c = 0; c < (kBN / 2) / 32; ++c) {
                     uint32_t w[32];
                     tmem_ld32(tbase + c * 32, w);
-                    if (c == (BN / 2) / 32 - 1) {
+                    if (c == (kBN / 2) / 32 - 1) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&bars.acc_empty[buf]);
@@ -542,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 stage_row(stage, lane, w);
                 fence_proxy_async_smem();
                 __syncwarp();
-                const int col0 = nb * BN + half * (BN / 2) + c * chunk_cols;
+                const int col0 = nb * kBN + half * (kBN / 2) + c * chunk_cols;
                 if (lane == 0 && row_in < M && col0 < N) {
                     if (epi == kEpiResidF32) tma_reduce_add_2d(&tmC, stage, col0, row0);
                     else tma_store_2d(&tmC, stage, col0, row0);
@@ -562,15 +581,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_coords(job_tile(t), num_m, num_n, &mb, &nb);
         const int rank = job_split(t);
         const int rows = M - mb * BM < BM ? M - mb * BM : BM;
-        const int total = rows * (BN / 4);                     // float4 pieces of the tile's live rows
+        const int total = rows * (kBN / 4);                    // float4 pieces of the tile's live rows
         const int per = (total + splits - 1) / splits;
         const int f_end = (rank + 1) * per < total ? (rank + 1) * per : total;
         const uint32_t pbase = smem_addr(smem);
         for (int f = rank * per + static_cast<int>(threadIdx.x); f < f_end; f += kThreads) {
-            const int r = f / (BN / 4), c4 = f % (BN / 4);
-            const int col = nb * BN + c4 * 4;
+            const int r = f / (kBN / 4), c4 = f % (kBN / 4);
+            const int col = nb * kBN + c4 * 4;
             if (col >= N) continue;
-            const uint32_t off = pbase + static_cast<uint32_t>((r * kPartStride + c4 * 4) * 4);
+            const uint32_t off = pbase + static_cast<uint32_t>((r * kPS + c4 * 4) * 4);
             // every split's load in flight at once (splits <= 16), then the
             // additions in split order
             float4 v[16];
@@ -676,6 +695,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int num_m2 = (M + 255) / 256, num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m2 * num_n;
     const int num_k = (K + BK - 1) / BK;
+    if (threadIdx.x == 32) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        prefetch_tmap(&tmC);
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES2; ++s) {
@@ -1001,12 +1025,12 @@ cudaError_t gemm_ex(const void* a, const void* b, void* c, const float* resid, i
             return cudaGetLastError();
         }
     }
-    static const cudaError_t attr_rc = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>,
+    static const cudaError_t attr_rc = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false, BN>,
                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (attr_rc != cudaSuccess) return attr_rc;
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    const cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES,
+    const cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false, BN>, dim3(grid), dim3(kThreads), SMEM_BYTES,
                                                 stream, ma, mb, mc, M, N, K, epi, 1, (K + BK - 1) / BK,
                                                 static_cast<void*>(nullptr), b_static, err);
     return e != cudaSuccess ? e : cudaGetLastError();
@@ -1097,16 +1121,42 @@ int csplit_cap() {
     return cap;
 }
 
-// Clusters of `size` CTAs of the cluster split-K kernel that can be resident
-// at once (0: none), queried once per size.
-int csplit_max_clusters(int size) {
-    static std::atomic<int> cache[17] = {};
-    if (cache[size].load(std::memory_order_relaxed) == 0) {
+// Output tile width of the cluster form for M rows: 128 for a single
+// M-block (the decode GEMMs: half the partial traffic of a 256-wide tile per
+// CTA, twice the tiles to spread the weights over), 256 otherwise. Measured
+// at M = 64 (d 1024, ffn 4096), microseconds per launch for widths 256 / 128
+// / 64: QKV 7.96 / 7.06 / 7.65, out-proj 8.28 / 6.69 / 6.78, W1 8.42 / 7.51 /
+// 7.93, W2 9.54 / 8.77 / 8.78 (64 leaves room for fewer splits, so each CTA
+// walks more of K). FERCUDA_SPLITK_BN = 64, 128 or 256 fixes the width.
+int csplit_bn(int M) {
+    static const int env = [] {
+        const char* e = std::getenv("FERCUDA_SPLITK_BN");
+        const int v = e ? std::atoi(e) : 0;
+        return (v == 64 || v == 128 || v == BN) ? v : 0;
+    }();
+    if (env) return env;
+    return M <= BM ? 128 : BN;
+}
+
+using ClusterKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, int, int, int, int, int, int, void*, int,
+                               uint32_t*);
+ClusterKernel cluster_kernel(int bn) {
+    return bn == 64 ? gemm_bf16_tc_kernel<true, 64> : bn == 128 ? gemm_bf16_tc_kernel<true, 128>
+                                                                : gemm_bf16_tc_kernel<true, BN>;
+}
+
+// Clusters of `size` CTAs of the cluster split-K kernel with tile width bn
+// that can be resident at once (0: none), queried once per (width, size);
+// also sets the kernel's shared-memory and cluster-size attributes.
+int csplit_max_clusters(int size, int bn) {
+    static std::atomic<int> cache[3][17] = {};
+    const int wi = bn == 64 ? 0 : bn == 128 ? 1 : 2;
+    const ClusterKernel kern = cluster_kernel(bn);
+    if (cache[wi][size].load(std::memory_order_relaxed) == 0) {
         int n = 0;
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e == cudaSuccess && size > 8)
-            e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e == cudaSuccess) {
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(static_cast<unsigned>(size * 16));
@@ -1119,32 +1169,35 @@ int csplit_max_clusters(int size) {
             at[0].val.clusterDim.z = 1;
             cfg.attrs = at;
             cfg.numAttrs = 1;
-            e = cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tc_kernel<true>, &cfg);
+            e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
         }
         if (e != cudaSuccess) {
             cudaGetLastError();
             n = 0;
         }
-        cache[size].store(n > 0 ? n : -1, std::memory_order_relaxed);
+        cache[wi][size].store(n > 0 ? n : -1, std::memory_order_relaxed);
     }
-    const int v = cache[size].load(std::memory_order_relaxed);
+    const int v = cache[wi][size].load(std::memory_order_relaxed);
     return v > 0 ? v : 0;
 }
 
 // Cluster split-K plan: the largest split count S <= 16 (each split whole
 // 64-deep k-blocks, S = ceil(num_k / ceil(num_k / S))) whose clusters of S
-// CTAs all fit on the GPU at once, one cluster per output tile. 1: no split
-// fits (the plain kernel runs); 0: the cluster form is off.
-int csplit_plan(int M, int N, int K, int* kps_out) {
+// CTAs all fit on the GPU at once, one cluster per output tile of width
+// *bn_out (csplit_bn). 1: no split fits (the plain kernel runs); 0: the
+// cluster form is off.
+int csplit_plan(int M, int N, int K, int* kps_out, int* bn_out) {
     const int cap = csplit_cap();
     const int num_k = (K + BK - 1) / BK;
+    const int bn = csplit_bn(M);
     *kps_out = num_k;
+    *bn_out = bn;
     if (cap == 0) return 0;
-    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
     for (int S = num_k < cap ? num_k : cap; S >= 2; --S) {
         const int kps = (num_k + S - 1) / S;
         if ((num_k + kps - 1) / kps != S) continue;
-        if (tiles <= csplit_max_clusters(S)) {
+        if (tiles <= csplit_max_clusters(S, bn)) {
             *kps_out = kps;
             return S;
         }
@@ -1159,8 +1212,8 @@ int csplit_plan(int M, int N, int K, int* kps_out) {
 // cluster form is switched off (FERCUDA_SPLITK_CLUSTER=0).
 extern "C" int fer_gemm_splitk_cluster_splits(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    int kps = 0;
-    return csplit_plan(M, N, K, &kps);
+    int kps = 0, bn = 0;
+    return csplit_plan(M, N, K, &kps, &bn);
 }
 
 // Split-K tensor-core GEMM for short M (decode steps): K is divided into
@@ -1191,7 +1244,8 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
         return cudaErrorInvalidValue;
     int kps = 0;
     if (splits <= 0) {
-        const int cs = csplit_plan(M, N, K, &kps);
+        int bn = BN;
+        const int cs = csplit_plan(M, N, K, &kps, &bn);
         if (cs == 1) return gemm_ex(a, b, c, epi == kEpiResidF32 ? static_cast<const float*>(c) : nullptr, M, N, K,
                                     epi, b_static, err, stream);
         if (cs >= 2) {
@@ -1199,7 +1253,7 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
             if (!make_map(&ma, a, static_cast<uint64_t>(M), static_cast<uint64_t>(K), BM) ||
                 !make_map(&mb, b, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BK))
                 return cudaErrorInvalidValue;
-            const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+            const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(static_cast<unsigned>(tiles * cs));
             cfg.blockDim = dim3(kThreads);
@@ -1216,8 +1270,8 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
             cfg.numAttrs = fer::host::pdl_enabled() ? 2 : 1;
             fer_pdl_note_launch();   // the kernel triggers its dependents either way
             // the C map is not used by the cluster form
-            const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<true>, ma, mb, ma, M, N, K, epi, cs,
-                                                     kps, c, b_static, err);
+            const cudaError_t e = cudaLaunchKernelEx(&cfg, cluster_kernel(bn), ma, mb, ma, M, N, K, epi, cs, kps, c,
+                                                     b_static, err);
             return e != cudaSuccess ? e : cudaGetLastError();
         }
     }
@@ -1232,12 +1286,12 @@ extern "C" cudaError_t fer_gemm_bf16_tc_splitk(const void* a, const void* b, voi
         !make_map(&mc, ws, static_cast<uint64_t>(splits) * mpad, static_cast<uint64_t>(N), 32,
                   CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
         return cudaErrorInvalidValue;
-    static const cudaError_t attr_rc = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false>,
+    static const cudaError_t attr_rc = cudaFuncSetAttribute(gemm_bf16_tc_kernel<false, BN>,
                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (attr_rc != cudaSuccess) return attr_rc;
     const int jobs = tiles * splits;
     const int grid = jobs < sm_count() ? jobs : sm_count();
-    cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false>, dim3(grid), dim3(kThreads), SMEM_BYTES, stream,
+    cudaError_t e = fer::host::launch_pdl(gemm_bf16_tc_kernel<false, BN>, dim3(grid), dim3(kThreads), SMEM_BYTES, stream,
                                           ma, mb, mc, M, N, K, static_cast<int>(kEpiF32), splits, kps,
                                           static_cast<void*>(nullptr), b_static, err);
     if (e == cudaSuccess) e = cudaGetLastError();

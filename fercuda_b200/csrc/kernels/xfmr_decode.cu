@@ -133,6 +133,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn(const __grid_constant__ 
     // first stage loads) before the programmatic launch wait; q and the new
     // row come from the kernel just before and are read after it.
     const bool early = d_len != nullptr;
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+    }
     if (!early) pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full[kStages];
