@@ -19,6 +19,7 @@
 // so the library needs no direct link to the driver library.
 #include "jit.hpp"
 
+#include <cuda.h>
 #include <nvrtc.h>
 
 #include <cerrno>
@@ -418,6 +419,48 @@ struct ChainParams {
     float v[2 * FER_CHAIN_MAX_OPS];
 };
 
+// Driver entry points for launching the chain kernels by CUfunction: a
+// library kernel launched through the runtime is looked up for the current
+// context on every launch; the function resolved once skips that.
+// FERCUDA_CHAIN_DRIVER_LAUNCH=0 keeps the runtime launch.
+struct DriverLaunch {
+    CUresult (*get)(CUfunction*, CUkernel) = nullptr;
+    CUresult (*launch)(const CUlaunchConfig*, CUfunction, void**, void**) = nullptr;
+    bool ok = false;
+};
+
+const DriverLaunch& driver_launch() {
+    static const DriverLaunch d = [] {
+        DriverLaunch r;
+        const char* e = std::getenv("FERCUDA_CHAIN_DRIVER_LAUNCH");
+        if (e && e[0] == '0') return r;
+        void* f0 = nullptr;
+        void* f1 = nullptr;
+        cudaDriverEntryPointQueryResult q0{}, q1{};
+        if (cudaGetDriverEntryPointByVersion("cuKernelGetFunction", &f0, 12000, cudaEnableDefault, &q0) ==
+                cudaSuccess &&
+            cudaGetDriverEntryPointByVersion("cuLaunchKernelEx", &f1, 12000, cudaEnableDefault, &q1) == cudaSuccess &&
+            q0 == cudaDriverEntryPointSuccess && q1 == cudaDriverEntryPointSuccess && f0 && f1) {
+            r.get = reinterpret_cast<CUresult (*)(CUfunction*, CUkernel)>(f0);
+            r.launch = reinterpret_cast<CUresult (*)(const CUlaunchConfig*, CUfunction, void**, void**)>(f1);
+            r.ok = true;
+        } else {
+            cudaGetLastError();
+        }
+        return r;
+    }();
+    return d;
+}
+
+// The driver function of a library kernel in the current context (null if
+// the driver path is off or the lookup fails).
+void* driver_function(cudaKernel_t k) {
+    const DriverLaunch& d = driver_launch();
+    if (!d.ok || !k) return nullptr;
+    CUfunction f = nullptr;
+    return d.get(&f, reinterpret_cast<CUkernel>(k)) == CUDA_SUCCESS ? reinterpret_cast<void*>(f) : nullptr;
+}
+
 }  // namespace
 
 int JitManager::sm() const {
@@ -732,6 +775,8 @@ fer_status_t JitManager::chain_kernels(const fer_chain_op_t* ops, uint32_t n_ops
         cudaGetLastError();
         return internal("generated chain kernel missing");
     }
+    ck.fv4 = driver_function(ck.v4);
+    ck.fs1 = driver_function(ck.s1);
     std::lock_guard<std::mutex> lk(mu_);
     auto res = chains_.emplace(sig, ck);
     *out = &res.first->second;
@@ -776,8 +821,26 @@ bool chain_early_enabled() {
     return on;
 }
 
-cudaError_t launch_pdl(const void* fn, unsigned grid, void** args, cudaStream_t stream) {
+cudaError_t launch_pdl(const void* fn, unsigned grid, void** args, cudaStream_t stream, void* drv = nullptr) {
     fer_pdl_note_launch();   // the chain kernels trigger their dependents however they are launched
+    if (drv) {
+        CUlaunchConfig cfg{};
+        cfg.gridDimX = grid;
+        cfg.gridDimY = 1;
+        cfg.gridDimZ = 1;
+        cfg.blockDimX = 256;
+        cfg.blockDimY = 1;
+        cfg.blockDimZ = 1;
+        cfg.sharedMemBytes = 0;
+        cfg.hStream = reinterpret_cast<CUstream>(stream);
+        CUlaunchAttribute attr[1];
+        attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        attr[0].value.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = chain_pdl_enabled() ? 1 : 0;
+        const CUresult r = fer::capi::driver_launch().launch(&cfg, reinterpret_cast<CUfunction>(drv), args, nullptr);
+        return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorLaunchFailure;
+    }
     if (!chain_pdl_enabled()) return cudaLaunchKernel(fn, dim3(grid), dim3(256), args, 0, stream);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
@@ -824,7 +887,7 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
         uint64_t g = (n4 + 511) / 512;   // two groups per thread before the wait
         if (g > cap) g = cap;
         void* args[] = {&a[0], &a[1], &a[2], &a[3], &out, &n4, &p, &early};
-        if (launch_pdl(reinterpret_cast<const void*>(ck.v4), static_cast<unsigned>(g), args, S.stream) !=
+        if (launch_pdl(reinterpret_cast<const void*>(ck.v4), static_cast<unsigned>(g), args, S.stream, ck.fv4) !=
             cudaSuccess) {
             cudaGetLastError();
             return internal("kernel launch failed");
@@ -836,7 +899,7 @@ fer_status_t launch_chain(Session& S, const ChainKernels& ck, const fer_chain_op
         uint64_t g = (n - done + 255) / 256;
         if (g > cap) g = cap;
         void* args[] = {&a[0], &a[1], &a[2], &a[3], &out, &lo, &hi, &p};
-        if (launch_pdl(reinterpret_cast<const void*>(ck.s1), static_cast<unsigned>(g), args, S.stream) !=
+        if (launch_pdl(reinterpret_cast<const void*>(ck.s1), static_cast<unsigned>(g), args, S.stream, ck.fs1) !=
             cudaSuccess) {
             cudaGetLastError();
             return internal("kernel launch failed");

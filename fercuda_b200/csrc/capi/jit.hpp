@@ -30,6 +30,10 @@ struct Module {
 struct ChainKernels {
     cudaKernel_t v4 = nullptr;   // 16-byte aligned streams, float4 per step
     cudaKernel_t s1 = nullptr;   // scalar tail / unaligned streams
+    // the same kernels as driver functions of this session's context,
+    // resolved once (null: launched through the runtime)
+    void* fv4 = nullptr;
+    void* fs1 = nullptr;
     std::shared_ptr<Module> mod;
 };
 
