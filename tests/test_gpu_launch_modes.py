@@ -55,3 +55,44 @@ def test_programmatic_launch_and_graphs_keep_the_bits():
         got = run_mode(extra)
         assert got[0] == base[0], extra
         assert got[0] == got[1] == got[2], extra
+
+
+CHAIN_CHILD = r"""
+import hashlib, json, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from fercuda_b200 import capi, synth
+n = (1 << 20) + 3                            # float4 body and scalar tail
+x = (synth.uniform01(0, n).astype(np.float32) * 8.0 - 4.0).astype(np.float32)
+with capi.Session(0, pool_bytes=256 << 20) as s:
+    bx, by = s.alloc(capi.FER_DTYPE_F32, [n]), s.alloc(capi.FER_DTYPE_F32, [n])
+    s.upload(bx, x)
+    fusion = capi.FER_JIT_INTENT_FUSION_RELU | capi.FER_JIT_INTENT_FUSION_MUL_SIGMOID_INPUT
+    out = []
+    for _ in range(3):
+        s.wait(s.affine(bx, by, n, 1.5, -0.25, fusion))
+        y = np.empty(n, np.float32)
+        s.download(by, y)
+        out.append(hashlib.sha256(y.tobytes()).hexdigest())
+    assert s.device_errors() == 0
+print(json.dumps(out))
+"""
+
+
+def test_chain_launch_paths_keep_the_bits():
+    """The fused elementwise chain launched through the driver by a function
+    resolved once (default), through the runtime (FERCUDA_CHAIN_DRIVER_LAUNCH=0)
+    and without programmatic launch (FERCUDA_CHAIN_PDL=0) gives the same
+    output bits."""
+    def run(extra):
+        env = dict(os.environ)
+        env.update(extra)
+        p = subprocess.run([sys.executable, "-c", CHAIN_CHILD, str(ROOT)], env=env, capture_output=True, text=True,
+                           timeout=300)
+        assert p.returncode == 0, p.stderr[-2000:]
+        return json.loads(p.stdout.strip().splitlines()[-1])
+
+    base = run({})
+    assert base[0] == base[1] == base[2]
+    assert run({"FERCUDA_CHAIN_DRIVER_LAUNCH": "0"}) == base
+    assert run({"FERCUDA_CHAIN_PDL": "0"}) == base
