@@ -876,8 +876,22 @@ def run_reference(args, rank):
         v, sample, cores = cls.cpu(threads)
         vals.append(v)
     v = float(np.mean(vals))
+    # one full step of the workload at the sampled rate (the sample itself is
+    # bounded: see cpu_baseline.sample)
+    d = cls.describe(args.gpus)
+    if cls is Transformer:
+        units = d["global_batch"] * d["seq_len"]                 # tokens
+    elif cls is Rows:
+        units = 8.0 * d["rows"] * d["cols"] / 1e9               # GB
+    elif cls is Chain:
+        units = 8.0 * d["n"] / 1e9                              # GB
+    else:
+        units = 2.0 * d["m"] * d["n"] * d["k"] / 1e12           # TFLOP
+    ms_step = units / v * 1e3 if v > 0 else None
     line = {"metric": cls.metric, "value": round(v, 4), "unit": cls.unit, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong" if cls is Transformer else "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 3) if ms_step else None,
+            "ms_per_step_note": "one full step at the sampled CPU rate",
+            "higher_is_better": True, "scaling": "strong" if cls is Transformer else "weak",
             "vs_baseline": None, "dtype": "bf16" if cls in (Transformer, Gemm) else "f32", "data": "synthetic",
             "config": cls.describe(args.gpus), "impl": "reference",
             "cpu_baseline": {"value": round(v, 4), "unit": cls.unit, "cores": cores, "kind": "port",
